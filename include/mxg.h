@@ -1,0 +1,137 @@
+/*
+ * mxg — B200-native (sm_100a) MXFP8 grouped GEMM: C ABI.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*) only; no torch
+ * types.  Every entry point is asynchronous on the given stream, returns 0 on
+ * success and a non-zero MXG_ERR_* code on a host-side validation or CUDA
+ * launch error.  Errors found on the device (inconsistent group offsets, a
+ * bounded wait that gave up) are recorded in a per-device error word read by
+ * mxg_get_device_error().  No entry point allocates memory: the caller passes
+ * a workspace whose size the *_workspace_size() functions return.
+ *
+ * Operand conventions (bytes are raw OCP MX formats):
+ *   e4m3  = float8_e4m3fn codes (uint8), e8m0 = biased power-of-two scale
+ *   (uint8, value 2^(b-127)); one scale per 32 consecutive elements along the
+ *   contraction dimension, stored row-major [rows, cols/32].  A null scale
+ *   pointer means unit scales (byte 0x7F).
+ *
+ * Reference interfaces replaced (indianspeedster/mxfp8-grouped-gemm):
+ *   mxg_grouped_fwd    <- fused_fwd.py:172-230   fused_grouped_fwd()
+ *   mxg_dense_fwd_kn   <- fwd_final.py:121-131   fwd_ge()
+ *   mxg_grouped_wgrad  <- wgrad_fused.py:34-112  wgrad_fused()/wgrad_kernel()
+ *   mxg_quantize_*     <- torchao triton_to_mxfp8_dim0/dim1 (mxfp8_rceil recipe),
+ *                         called by the reference's MoE path (port_mxfp8.py:43-49,207-212)
+ */
+#ifndef MXG_H_
+#define MXG_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MXG_API __attribute__((visibility("default")))
+#else
+#define MXG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define MXG_OK 0
+#define MXG_ERR_INVALID_ARGUMENT 1    /* null pointer, negative size, bad enum */
+#define MXG_ERR_BAD_SHAPE 2           /* dims not multiples of 32, too large    */
+#define MXG_ERR_MISALIGNED 3          /* base pointer not 16-byte aligned       */
+#define MXG_ERR_WORKSPACE_TOO_SMALL 4
+#define MXG_ERR_CUDA 5                /* a CUDA runtime/driver call failed      */
+#define MXG_ERR_DEVICE_TIMEOUT 6      /* a device-side bounded wait gave up     */
+#define MXG_ERR_BAD_OFFSETS 7         /* group offsets inconsistent (device)    */
+#define MXG_ERR_UNSUPPORTED_DEVICE 8  /* not an sm_100 (B200-class) GPU          */
+#define MXG_ERR_TOO_MANY_GROUPS 9
+
+/* ---- group-offset conventions (the reference uses all three) ------------ */
+#define MXG_OFFS_LEADING_ZERO 0 /* [E+1], offs[0]==0, group e = [offs[e], offs[e+1])   fused_fwd.py:7 */
+#define MXG_OFFS_CUMULATIVE 1   /* [E],   group e = [offs[e-1], offs[e])                fwd_final.py:170 */
+#define MXG_OFFS_SIZES 2        /* [E],   group e has offs[e] rows                      wgrad_fused.py:37 */
+#define MXG_OFFS_AUTO 3         /* [E+1] -> leading zero; [E] -> cumulative when
+                                   non-decreasing with last == M, sizes when they
+                                   sum to M, else MXG_ERR_BAD_OFFSETS (device)       */
+
+#define MXG_DTYPE_BF16 0
+#define MXG_DTYPE_F32 1
+
+#define MXG_MAX_GROUPS 256
+
+/* Human-readable text for a status code (static storage). */
+MXG_API const char* mxg_error_string(int code);
+
+/* Library version, major*10000 + minor*100 + patch. */
+MXG_API int mxg_version(void);
+
+/* Read (and optionally clear) the current device's error word.  Synchronises
+ * the device.  *code receives 0 or the first MXG_ERR_* a kernel recorded. */
+MXG_API int mxg_get_device_error(int* code, int clear);
+
+/* ---- MXFP8 quantisers (RCEIL E8M0 scales, RNE e4m3, saturating) ------------
+ * Row-wise 1x32: x [rows, cols] bf16 -> q [rows, cols] e4m3, scales [rows, cols/32].
+ * cols % 32 == 0.  Replaces torchao triton_to_mxfp8_dim0 (reference MoE forward
+ * operands, memory/2026-06-09.md:10,20). */
+MXG_API int mxg_quantize_rowwise(const void* x_bf16, int64_t rows, int64_t cols, void* q_e4m3,
+                         void* scales_e8m0, void* stream);
+
+/* Column-wise 32x1 with transposed output: x [rows, cols] bf16 ->
+ * qt [cols, rows] e4m3, scales_t [cols, rows/32].  rows % 32 == 0, cols even.
+ * Produces the token-contiguous wgrad operands go (N, M) / ia (K, M) of
+ * wgrad_fused.py:35-39; replaces torchao triton_to_mxfp8_dim1. */
+MXG_API int mxg_quantize_colwise(const void* x_bf16, int64_t rows, int64_t cols, void* qt_e4m3,
+                         void* scales_t_e8m0, void* stream);
+
+/* ---- grouped forward: y[rows of e] = x[rows of e] . W[e]^T -----------------
+ * a [m, k] e4m3, a_scales [m, k/32]; w [num_groups, n, k] e4m3,
+ * w_scales [num_groups, n, k/32]; offs int32 device array (see MXG_OFFS_*; may
+ * be null when num_groups == 1, meaning one group of all m rows); out [m, n]
+ * bf16 or f32.  Rows of out outside every group are written as zero.
+ * k % 32 == 0, num_groups <= MXG_MAX_GROUPS.
+ * Replaces fused_fwd.py:172-230 fused_grouped_fwd (which assumed equal
+ * groups, fused_fwd.py:48; here groups may be any size, including empty). */
+MXG_API size_t mxg_grouped_fwd_workspace_size(int num_groups, int64_t m, int64_t n, int64_t k);
+MXG_API int mxg_grouped_fwd(const void* a, const void* a_scales, const void* w, const void* w_scales,
+                    const int32_t* offs, int offs_len, int offs_kind, int num_groups, int64_t m,
+                    int64_t n, int64_t k, void* out, int out_dtype, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* ---- dense forward with a K x N weight: out[m, n] = x[m, k] . w[k, n] -------
+ * Unit scales (the reference's fwd_ge passes none, fwd_final.py:101-106).
+ * Replaces fwd_final.py:121-131 fwd_ge. */
+MXG_API size_t mxg_dense_fwd_kn_workspace_size(int64_t m, int64_t n, int64_t k);
+MXG_API int mxg_dense_fwd_kn(const void* x, const void* w_kn, int64_t m, int64_t n, int64_t k, void* out,
+                     int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- grouped weight gradient: dW[e] = go[:, tokens of e] . ia[:, tokens of e]^T
+ * go [n, m] e4m3 (token-contiguous), go_scales [n, m/32]; ia [k, m] e4m3,
+ * ia_scales [k, m/32]; out [num_groups, n, k] bf16 or f32 (empty groups -> 0).
+ * Group boundaries must be multiples of 32 tokens (one scale block never
+ * straddles two experts); m % 32 == 0, k % 16 == 0.
+ * Replaces wgrad_fused.py:34-112 (which stacked per-expert copies and assumed
+ * equal groups, wgrad_fused.py:46-62; here the contraction reads each
+ * expert's token range in place). */
+MXG_API size_t mxg_grouped_wgrad_workspace_size(int num_groups, int64_t m, int64_t n, int64_t k);
+MXG_API int mxg_grouped_wgrad(const void* go, const void* go_scales, const void* ia,
+                      const void* ia_scales, const int32_t* offs, int offs_len, int offs_kind,
+                      int num_groups, int64_t m, int64_t n, int64_t k, void* out, int out_dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- byte transpose: dst [cols, rows] = src [rows, cols]^T (uint8) ----------- */
+MXG_API int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, void* dst, void* stream);
+
+/* Test hook: the next grouped GEMM launch on this device waits on a barrier
+ * nothing arrives on, with the given limit in nanoseconds, so the bounded
+ * wait runs out and records MXG_ERR_DEVICE_TIMEOUT.  0 disables. */
+MXG_API int mxg_debug_inject_stall(int64_t timeout_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXG_H_ */

@@ -1,0 +1,877 @@
+// Grouped MXFP8 GEMM for sm_100a (tcgen05 block-scaled MMA, TMA, TMEM).
+//
+// One kernel serves both hot-path contractions.  Each computes, per group e,
+//     D[i, j] = sum_k A[i, k] * B[j, k]       (both operands K-contiguous)
+// with one E8M0 scale per 32 k for every row of A and of B:
+//   forward (fused_fwd.py:172-230):  A = W[e] rows (features), B = token rows
+//       of x in group e, k = hidden; stored transposed into y[token, feature]
+//       ("swap AB": tokens sit on the MMA N side, so a tile's token count can
+//       follow the group size exactly instead of padding to 128).
+//   wgrad (wgrad_fused.py:34-112):   A = go rows (dW rows), B = ia rows (dW
+//       columns), k = the group's token range read in place from the
+//       token-contiguous operands; stored row-major into dW[e].
+//
+// Pipeline per persistent CTA (one per SM, 192 threads):
+//   warp 4  TMA producer: A tile 128 x 128 B, B tile up to 240 x 128 B
+//           (128-byte swizzle) and the two pre-packed scale chunks, into a
+//           4-stage shared-memory ring (mbarrier tx counts).
+//   warp 5  TMEM owner + single-thread MMA issuer: copies the stage's scale
+//           factors shared->TMEM (tcgen05.cp 32x128b.warpx4) and issues
+//           tcgen05.mma kind::mxf8f6f4.block_scale (M=128, N<=240, K=32).
+//   warps 0-3 epilogue: tcgen05.ld 32x32b, convert, store; the accumulator
+//           is double-buffered in TMEM so the epilogue of tile i overlaps
+//           the main loop of tile i+1.
+// Every mbarrier wait is bounded (MXG_ERR_DEVICE_TIMEOUT, then unwind).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "mxg.h"
+#include "mxg_internal.h"
+#include "mxg_ptx.cuh"
+
+namespace mxg {
+
+constexpr int kBM = 128;                 // A rows per tile (MMA M)
+constexpr int kBNMax = 240;              // max B rows per tile (MMA N)
+constexpr int kBK = 128;                 // contraction bytes per stage
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK;       // 16 KiB
+constexpr int kBBytes = kBNMax * kBK;    // 30 KiB
+constexpr int kSfaBytes = 512;           // 128 rows x 4 scales, UTCCP layout
+constexpr int kSfbBytes = 1024;          // 2 x (128 rows x 4 scales)
+constexpr uint32_t kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccStride = 256;     // accumulator buffer i at column 256*i
+constexpr uint32_t kSfaCol = 240;        // 4 columns
+constexpr uint32_t kSfbCol = 244;        // 8 columns
+
+enum { MODE_FWD = 0, MODE_WGRAD = 1 };
+
+// ---- scheduler output (int32 words in the workspace) ------------------------
+//   [0] tiles  [1] A scale chunks  [2] B scale chunks  [3] first row after the
+//   last group (forward zero-fill)  [4..7] reserved, then the arrays below.
+struct MetaView {
+  int* base;
+  int E;
+  __host__ __device__ int* tile_start() const { return base + 8; }           // E+1
+  __host__ __device__ int* g_start() const { return base + 8 + (E + 1); }    // E
+  __host__ __device__ int* g_len() const { return g_start() + E; }          // E
+  __host__ __device__ int* g_nt() const { return g_len() + E; }             // E
+  __host__ __device__ int* g_kb() const { return g_nt() + E; }              // E
+  __host__ __device__ int* g_asf() const { return g_kb() + E; }             // E+1
+  __host__ __device__ int* g_bsf() const { return g_asf() + E + 1; }        // E+1
+  __host__ __device__ static size_t words(int E) { return 8 + 7 * size_t(E) + 3; }
+};
+
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Balanced split of `ext` rows into `nt` tiles of whole 16-row units (each
+// at most kBNMax rows).  Returns the first row and the row count of tile `i`.
+__host__ __device__ inline void split_rows(int ext, int nt, int i, int& n0, int& nlen) {
+  const int units = (ext + 15) / 16;
+  const int q = units / nt, r = units % nt;
+  const int u0 = i * q + (i < r ? i : r);
+  const int ul = q + (i < r ? 1 : 0);
+  n0 = 16 * u0;
+  nlen = min(16 * ul, ext - n0);
+}
+
+// ---------------------------------------------------------------- scheduler
+struct SchedArgs {
+  const int32_t* offs;
+  int offs_len;
+  int offs_kind;
+  int E;
+  int M;
+  int mode;
+  int n_out;   // A-side rows per group
+  int n_ext;   // wgrad: B-side rows (dW columns)
+  int k_fwd;   // forward contraction length
+  int* meta;
+  int* err;
+};
+
+__device__ int block_excl_scan(int v, int* total, int* warp_sums) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < (blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < (blockDim.x >> 5)) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  const int before = (warp ? warp_sums[warp - 1] : 0) + x - v;
+  *total = warp_sums[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return before;
+}
+
+__global__ void __launch_bounds__(MXG_MAX_GROUPS) schedule_kernel(SchedArgs a) {
+  __shared__ int raw[MXG_MAX_GROUPS + 1];
+  __shared__ int warp_sums[32];
+  __shared__ int kind_s;
+  const int tid = threadIdx.x, E = a.E;
+  const int L = a.offs ? a.offs_len : 0;
+  for (int i = tid; i < L && i <= MXG_MAX_GROUPS; i += blockDim.x) raw[i] = a.offs[i];
+  if (tid == 0) kind_s = a.offs ? a.offs_kind : -1;
+  __syncthreads();
+  bool bad = false;
+  int kind = kind_s;
+  if (kind == MXG_OFFS_AUTO) {
+    if (L == E + 1) {
+      kind = MXG_OFFS_LEADING_ZERO;
+    } else {
+      const bool mono = (tid < E - 1) ? raw[tid] <= raw[tid + 1] : true;
+      const bool all_mono = __syncthreads_and(mono);
+      if (all_mono && raw[E - 1] == a.M) {
+        kind = MXG_OFFS_CUMULATIVE;
+      } else {
+        int tot;
+        (void)block_excl_scan(tid < E ? raw[tid] : 0, &tot, warp_sums);
+        const bool nonneg = __syncthreads_and(tid < E ? raw[tid] >= 0 : true);
+        kind = (nonneg && tot == a.M) ? MXG_OFFS_SIZES : -2;
+      }
+    }
+  }
+  // group starts and lengths
+  int start = 0, len = 0;
+  if (kind == -1) {  // no offsets: one group of all rows
+    start = 0;
+    len = (tid == 0) ? a.M : 0;
+  } else if (kind == MXG_OFFS_LEADING_ZERO) {
+    if (tid < E) {
+      start = raw[tid];
+      len = raw[tid + 1] - raw[tid];
+    }
+    if (tid == 0 && raw[0] != 0) bad = true;
+  } else if (kind == MXG_OFFS_CUMULATIVE) {
+    if (tid < E) {
+      start = tid ? raw[tid - 1] : 0;
+      len = raw[tid] - start;
+    }
+  } else if (kind == MXG_OFFS_SIZES) {
+    int tot;
+    const int sz = tid < E ? raw[tid] : 0;
+    start = block_excl_scan(sz, &tot, warp_sums);
+    len = sz;
+  } else {
+    bad = true;
+  }
+  if (tid < E) {
+    if (len < 0 || start < 0 || start + len > a.M) bad = true;
+    if (a.mode == MODE_WGRAD && ((start & 31) || (len & 31))) bad = true;
+  }
+  const bool any_bad = __syncthreads_or(bad);
+  // per-group work counts
+  int nt = 0, kb = 0, tiles = 0, asf = 0, bsf = 0;
+  const int mb = ceil_div(a.n_out, kBM);
+  if (tid < E && !any_bad) {
+    if (a.mode == MODE_FWD) {
+      nt = ceil_div(len, kBNMax);
+      kb = ceil_div(a.k_fwd, kBK);
+    } else {
+      nt = ceil_div(a.n_ext, kBNMax);
+      kb = ceil_div(len, kBK);
+    }
+    tiles = mb * nt;
+    asf = mb * kb;
+    bsf = nt * kb;
+  }
+  int t_tot, a_tot, b_tot;
+  const int t0 = block_excl_scan(tiles, &t_tot, warp_sums);
+  const int a0 = block_excl_scan(asf, &a_tot, warp_sums);
+  const int b0 = block_excl_scan(bsf, &b_tot, warp_sums);
+  MetaView mv{a.meta, E};
+  if (tid < E) {
+    mv.tile_start()[tid] = t0;
+    mv.g_start()[tid] = any_bad ? 0 : start;
+    mv.g_len()[tid] = any_bad ? 0 : len;
+    mv.g_nt()[tid] = nt;
+    mv.g_kb()[tid] = kb;
+    mv.g_asf()[tid] = a0;
+    mv.g_bsf()[tid] = b0;
+  }
+  // last group's end = first uncovered row (groups are contiguous from row 0)
+  int end_local = (tid < E) ? start + len : 0;
+  for (int o = 16; o > 0; o >>= 1) end_local = max(end_local, __shfl_xor_sync(0xffffffffu, end_local, o));
+  if ((tid & 31) == 0) warp_sums[tid >> 5] = end_local;
+  __syncthreads();
+  if (tid == 0) {
+    int end_all = 0;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) end_all = max(end_all, warp_sums[w]);
+    mv.tile_start()[E] = t_tot;
+    mv.g_asf()[E] = a_tot;
+    mv.g_bsf()[E] = b_tot;
+    a.meta[0] = any_bad ? 0 : t_tot;
+    a.meta[1] = any_bad ? 0 : a_tot;
+    a.meta[2] = any_bad ? 0 : b_tot;
+    a.meta[3] = any_bad ? 0 : end_all;
+    if (any_bad) atomicCAS(a.err, 0, MXG_ERR_BAD_OFFSETS);
+  }
+}
+
+// ---------------------------------------------------------------- scale packing
+// Re-lays the row-major E8M0 scales of one operand into 512-byte chunks, one
+// per (128 rows, 128 contraction elements): byte (r%32)*16 + (r/32)*4 + kk
+// for row r and 32-element block kk -- the shared-memory layout that
+// tcgen05.cp 32x128b.warpx4 turns into the TMEM scale-factor layout.  Rows or
+// blocks outside the operand are filled with 0x7F (unit scale; those rows and
+// steps are never stored or issued).
+struct PackArgs {
+  const int* meta;
+  int E;
+  int mode;
+  int side;             // 0: A operand (128-row chunks), 1: B operand (2 x 128 rows)
+  const uint8_t* src;   // row-major scales, null -> unit scales
+  int64_t src_ld;       // bytes per scale row
+  uint8_t* dst;
+  int n_out;
+  int n_ext;
+  int k_fwd;
+};
+
+__global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
+  __shared__ int base_s[MXG_MAX_GROUPS + 1];
+  MetaView mv{const_cast<int*>(p.meta), p.E};
+  const int* base = p.side == 0 ? mv.g_asf() : mv.g_bsf();
+  for (int i = threadIdx.x; i <= p.E; i += blockDim.x) base_s[i] = base[i];
+  __syncthreads();
+  const int total = base_s[p.E];
+  const int chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
+  const int rows_per_chunk = p.side == 0 ? 128 : 256;
+  const int r = threadIdx.x;
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    int lo = 0, hi = p.E - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (base_s[mid] <= c) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo;
+    const int local = c - base_s[e];
+    const int kbn = mv.g_kb()[e];
+    const int blk = local / kbn, kb = local - blk * kbn;
+    const int gstart = mv.g_start()[e], glen = mv.g_len()[e];
+    int row0, valid, col0, col_end;
+    if (p.side == 0) {
+      row0 = (p.mode == MODE_FWD ? e * p.n_out : 0) + blk * kBM;
+      valid = min(kBM, p.n_out - blk * kBM);
+    } else {
+      const int ext = p.mode == MODE_FWD ? glen : p.n_ext;
+      int n0, nlen;
+      split_rows(ext, mv.g_nt()[e], blk, n0, nlen);
+      row0 = (p.mode == MODE_FWD ? gstart : 0) + n0;
+      valid = nlen;
+    }
+    if (p.mode == MODE_FWD) {
+      col0 = kb * 4;
+      col_end = p.k_fwd / 32;
+    } else {
+      col0 = gstart / 32 + kb * 4;
+      col_end = (gstart + glen) / 32;
+    }
+    if (r < rows_per_chunk) {
+      uint32_t word = 0x7F7F7F7Fu;
+      if (p.src && r < valid) {
+        const uint8_t* srow = p.src + int64_t(row0 + r) * p.src_ld;
+        word = 0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int col = col0 + kk;
+          const uint32_t v = col < col_end ? uint32_t(srow[col]) : 0x7Fu;
+          word |= v << (8 * kk);
+        }
+      }
+      const int half = r >> 7, rr = r & 127;
+      uint8_t* d = p.dst + int64_t(c) * chunk_bytes + half * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+      *reinterpret_cast<uint32_t*>(d) = word;
+    }
+  }
+}
+
+// Forward: rows [meta[3], M) belong to no group -> write zeros.
+__global__ void zero_tail_kernel(const int* meta, uint8_t* out, int64_t M, int64_t row_bytes) {
+  const int64_t first = meta[3];
+  if (first >= M) return;
+  const int64_t beg = first * row_bytes, end = M * row_bytes;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = beg + (int64_t(blockIdx.x) * blockDim.x + threadIdx.x); i < end; i += stride)
+    out[i] = 0;
+}
+
+// ---------------------------------------------------------------- GEMM kernel
+struct GemmArgs {
+  const int* meta;
+  const uint8_t* sfa_pack;
+  const uint8_t* sfb_pack;
+  void* out;
+  int out_dtype;
+  int E;
+  int n_out;     // A rows per group (forward: features N; wgrad: dW rows N)
+  int n_ext;     // wgrad: dW columns K
+  int k_fwd;     // forward contraction K
+  int64_t ldo;   // output row stride in elements
+  int* err;
+  uint64_t timeout_ns;
+  int stall_test;
+};
+
+struct __align__(1024) SmemLayout {
+  uint8_t a[kStages][kABytes];
+  uint8_t b[kStages][kBBytes];
+  uint8_t sfa[kStages][kSfaBytes];
+  uint8_t sfb[kStages][kSfbBytes];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint64_t never;
+  uint32_t tmem_base;
+  int abort_flag;
+  int num_tiles;
+  int tile_start[MXG_MAX_GROUPS + 1];
+  int g_start[MXG_MAX_GROUPS];
+  int g_len[MXG_MAX_GROUPS];
+  int g_nt[MXG_MAX_GROUPS];
+  int g_kb[MXG_MAX_GROUPS];
+  int g_asf[MXG_MAX_GROUPS + 1];
+  int g_bsf[MXG_MAX_GROUPS + 1];
+};
+constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;
+
+struct TileInfo {
+  int e, mb, nt, n0, nlen, kb_count, klen, k0, a_row, b_row, sfa0, sfb0;
+};
+
+template <int MODE>
+__device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmArgs& g, int t) {
+  TileInfo ti;
+  int lo = 0, hi = g.E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s.tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  ti.e = lo;
+  const int local = t - s.tile_start[lo];
+  const int nt_count = s.g_nt[lo];
+  ti.mb = local / nt_count;
+  ti.nt = local - ti.mb * nt_count;
+  const int ext = MODE == MODE_FWD ? s.g_len[lo] : g.n_ext;
+  split_rows(ext, nt_count, ti.nt, ti.n0, ti.nlen);
+  ti.kb_count = s.g_kb[lo];
+  if (MODE == MODE_FWD) {
+    ti.klen = g.k_fwd;
+    ti.k0 = 0;
+    ti.a_row = lo * g.n_out + ti.mb * kBM;
+    ti.b_row = s.g_start[lo] + ti.n0;
+  } else {
+    ti.klen = s.g_len[lo];
+    ti.k0 = s.g_start[lo];
+    ti.a_row = ti.mb * kBM;
+    ti.b_row = ti.n0;
+  }
+  ti.sfa0 = s.g_asf[lo] + ti.mb * ti.kb_count;
+  ti.sfb0 = s.g_bsf[lo] + ti.nt * ti.kb_count;
+  return ti;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Epilogue store of 32 accumulator columns [c0, c0+32) held by this thread
+// (TMEM lane = `row` of the tile).
+template <int MODE>
+__device__ __forceinline__ void store_chunk(const GemmArgs& g, const TileInfo& ti, int row, int c0,
+                                            const uint32_t (&v)[32], bool zero) {
+  const int ncols = min(32, ti.nlen - c0);
+  if (MODE == MODE_FWD) {
+    const int f = ti.mb * kBM + row;
+    if (f >= g.n_out) return;
+    const int64_t tok0 = int64_t(ti.b_row) + c0;
+    if (g.out_dtype == MXG_DTYPE_BF16) {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + tok0 * g.ldo + f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) o[int64_t(j) * g.ldo] = __float2bfloat16_rn(zero ? 0.f : __uint_as_float(v[j]));
+    } else {
+      float* o = reinterpret_cast<float*>(g.out) + tok0 * g.ldo + f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) o[int64_t(j) * g.ldo] = zero ? 0.f : __uint_as_float(v[j]);
+    }
+  } else {
+    const int r = ti.mb * kBM + row;
+    if (r >= g.n_out) return;
+    const int64_t off = (int64_t(ti.e) * g.n_out + r) * g.ldo + ti.n0 + c0;
+    if (g.out_dtype == MXG_DTYPE_F32) {
+      float* o = reinterpret_cast<float*>(g.out) + off;
+      if (ncols == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 q = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                          : make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                        __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+          *reinterpret_cast<float4*>(o + j) = q;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) o[j] = zero ? 0.f : __uint_as_float(v[j]);
+      }
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + off;
+      if (ncols == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 q;
+          if (zero) {
+            q = make_uint4(0, 0, 0, 0);
+          } else {
+            q.x = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+            q.y = pack_bf16x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+            q.z = pack_bf16x2(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
+            q.w = pack_bf16x2(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
+          }
+          *reinterpret_cast<uint4*>(o + j) = q;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < ncols) o[j] = __float2bfloat16_rn(zero ? 0.f : __uint_as_float(v[j]));
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemLayout& s = *reinterpret_cast<SmemLayout*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  MetaView mv{const_cast<int*>(g.meta), g.E};
+  for (int i = threadIdx.x; i <= g.E; i += kThreads) {
+    s.tile_start[i] = mv.tile_start()[i];
+    s.g_asf[i] = mv.g_asf()[i];
+    s.g_bsf[i] = mv.g_bsf()[i];
+  }
+  for (int i = threadIdx.x; i < g.E; i += kThreads) {
+    s.g_start[i] = mv.g_start()[i];
+    s.g_len[i] = mv.g_len()[i];
+    s.g_nt[i] = mv.g_nt()[i];
+    s.g_kb[i] = mv.g_kb()[i];
+  }
+  if (threadIdx.x == 0) {
+    s.num_tiles = g.meta[0];
+    s.abort_flag = 0;
+  }
+  if (warp == 4 && lane == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&s.full[i]), 1);
+      mbar_init(smem_u32(&s.empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&s.acc_full[i]), 1);
+      mbar_init(smem_u32(&s.acc_empty[i]), 4 * 32);
+    }
+    mbar_init(smem_u32(&s.drain), 1);
+    mbar_init(smem_u32(&s.never), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&s.tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  const int num_tiles = s.num_tiles;
+  WaitCtl wc{&s.abort_flag, g.err, g.timeout_ns};
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile<MODE>(s, g, t);
+        for (int kb = 0; kb < ti.kb_count; ++kb) {
+          if (!mbar_wait(smem_u32(&s.empty[stage]), phase ^ 1u, wc)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&s.full[stage]);
+          mbar_arrive_expect_tx(fb, kStageTx);
+          const int x = ti.k0 + kb * kBK;
+          tma_load_2d(smem_u32(s.a[stage]), &tmA, x, ti.a_row, fb);
+          tma_load_2d(smem_u32(s.b[stage]), &tmB, x, ti.b_row, fb);
+          bulk_load(smem_u32(s.sfa[stage]), g.sfa_pack + int64_t(ti.sfa0 + kb) * kSfaBytes,
+                    kSfaBytes, fb);
+          bulk_load(smem_u32(s.sfb[stage]), g.sfb_pack + int64_t(ti.sfb0 + kb) * kSfbBytes,
+                    kSfbBytes, fb);
+          armed |= 1u << stage;
+          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {  // unwinding: let the copies already issued land first
+        for (int i = 0; i < kStages; ++i)
+          if (armed & (1u << i)) mbar_drain(smem_u32(&s.full[i]), (armed_par >> i) & 1u, 20000000ull);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true, issued = false;
+      if (g.stall_test) ok = mbar_wait(smem_u32(&s.never), 0, wc);
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile<MODE>(s, g, t);
+        if (ti.kb_count == 0) continue;
+        if (!mbar_wait(smem_u32(&s.acc_empty[acc]), acc_phase ^ 1u, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kAccStride;
+        const uint32_t n_mma = uint32_t(ti.nlen + 15) & ~15u;
+        const uint32_t idesc0 = make_idesc_mxf8(kBM, n_mma);
+        const uint32_t sfa_t = tmem_base + kSfaCol, sfb_t = tmem_base + kSfbCol;
+        for (int kb = 0; kb < ti.kb_count; ++kb) {
+          if (!mbar_wait(smem_u32(&s.full[stage]), phase, wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfa_s = smem_u32(s.sfa[stage]), sfb_s = smem_u32(s.sfb[stage]);
+          tc_cp_32x128b_warpx4(sfa_t, sdesc_sf_chunk(sfa_s));
+          tc_cp_32x128b_warpx4(sfb_t, sdesc_sf_chunk(sfb_s));
+          tc_cp_32x128b_warpx4(sfb_t + 4, sdesc_sf_chunk(sfb_s + 512));
+          const int rem = ti.klen - kb * kBK;
+          const int nk = rem >= kBK ? 4 : rem / 32;
+          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(s.a[stage]));
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(s.b[stage]));
+          for (int kk = 0; kk < nk; ++kk) {
+            tc_mma_mxf8(d_tmem, adesc + uint64_t(2 * kk), bdesc + uint64_t(2 * kk),
+                        idesc_with_sf_id(idesc0, kk, kk), sfa_t | (uint32_t(kk) << 30),
+                        sfb_t | (uint32_t(kk) << 30), (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&s.empty[stage]));
+          issued = true;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&s.acc_full[acc]));
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (issued) {  // every MMA done before TMEM is released
+        tc_commit(smem_u32(&s.drain));
+        mbar_drain(smem_u32(&s.drain), 0, 50000000ull);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 0-3)
+    const int row = warp * 32 + lane;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile<MODE>(s, g, t);
+      uint32_t v[32];
+      if (ti.kb_count == 0) {  // empty group (wgrad): dW[e] = 0
+        for (int c0 = 0; c0 < ti.nlen; c0 += 32) store_chunk<MODE>(g, ti, row, c0, v, true);
+        continue;
+      }
+      bool ok = mbar_wait(smem_u32(&s.acc_full[acc]), acc_phase, wc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (uint32_t(warp * 32) << 16) + acc * kAccStride;
+      for (int c0 = 0; c0 < ti.nlen; c0 += 32) {
+        tmem_ld_32x32b_x32(tb + uint32_t(c0), v);
+        tmem_ld_wait();
+        store_chunk<MODE>(g, ti, row, c0, v, false);
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&s.acc_empty[acc]));
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor [rows, cols] (cols contiguous), box {128 bytes, box_rows},
+// 128-byte swizzle; out-of-range elements read as zero.
+static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return MXG_ERR_CUDA;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols)};
+  cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
+}
+
+struct WsLayout {
+  size_t meta_off, sfa_off, sfb_off, total;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static WsLayout ws_layout(int mode, int E, int64_t M, int64_t n_out, int64_t n_ext, int64_t K) {
+  const int64_t mb = (n_out + kBM - 1) / kBM;
+  int64_t asf, bsf;
+  if (mode == MODE_FWD) {
+    const int64_t kb = (K + kBK - 1) / kBK;
+    asf = int64_t(E) * mb * kb;
+    bsf = kb * ((M + int64_t(kBNMax - 1) * E) / kBNMax + 1);
+  } else {
+    const int64_t kbs = (M + int64_t(kBK - 1) * E) / kBK + 1;
+    const int64_t nt = (n_ext + kBNMax - 1) / kBNMax;
+    asf = mb * kbs;
+    bsf = nt * kbs;
+  }
+  WsLayout w;
+  w.meta_off = 0;
+  w.sfa_off = align_up(MetaView::words(E) * 4, 1024);
+  w.sfb_off = align_up(w.sfa_off + size_t(asf) * kSfaBytes, 1024);
+  w.total = align_up(w.sfb_off + size_t(bsf) * kSfbBytes, 1024);
+  return w;
+}
+
+static int configure_kernels() {
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MXG_ERR_CUDA;
+  if (dev < 64 && done[dev]) return MXG_OK;
+  if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_FWD>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
+    return MXG_ERR_CUDA;
+  if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_WGRAD>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
+    return MXG_ERR_CUDA;
+  if (dev < 64) done[dev] = true;
+  return MXG_OK;
+}
+
+static constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per wait
+
+// Shared launcher for both modes.
+//   A operand: a_ptr [a_rows, kc] e4m3, scales a_sc [a_rows, kc/32]
+//   B operand: b_ptr [b_rows, kc] e4m3, scales b_sc [b_rows, kc/32]
+static int launch_grouped(int mode, const void* a_ptr, const void* a_sc, int64_t a_rows,
+                          const void* b_ptr, const void* b_sc, int64_t b_rows, int64_t kc,
+                          const int32_t* offs, int offs_len, int offs_kind, int E, int64_t M,
+                          int64_t n_out, int64_t n_ext, void* out, int out_dtype, int64_t ldo,
+                          void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const WsLayout L = ws_layout(mode, E, M, n_out, n_ext, kc);
+  if (ws_bytes < L.total) return MXG_ERR_WORKSPACE_TOO_SMALL;
+  int st = check_device();
+  if (st) return st;
+  st = configure_kernels();
+  if (st) return st;
+  uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+  int* meta = reinterpret_cast<int*>(wsb + L.meta_off);
+  uint8_t* sfa = wsb + L.sfa_off;
+  uint8_t* sfb = wsb + L.sfb_off;
+  int* err = device_error_word();
+  if (!err) return MXG_ERR_CUDA;
+
+  CUtensorMap tmA, tmB;
+  st = make_tmap(&tmA, a_ptr, a_rows, kc, kBM);
+  if (st) return st;
+  st = make_tmap(&tmB, b_ptr, b_rows, kc, kBNMax);
+  if (st) return st;
+
+  SchedArgs sa{offs, offs_len, offs_kind, E, int(M), mode, int(n_out), int(n_ext), int(kc), meta, err};
+  schedule_kernel<<<1, MXG_MAX_GROUPS, 0, stream>>>(sa);
+
+  const int sms = num_sms();
+  PackArgs pa{meta, E, mode, 0, reinterpret_cast<const uint8_t*>(a_sc), kc / 32, sfa,
+              int(n_out), int(n_ext), int(kc)};
+  pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pa);
+  PackArgs pb = pa;
+  pb.side = 1;
+  pb.src = reinterpret_cast<const uint8_t*>(b_sc);
+  pb.dst = sfb;
+  pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+
+  GemmArgs ga;
+  ga.meta = meta;
+  ga.sfa_pack = sfa;
+  ga.sfb_pack = sfb;
+  ga.out = out;
+  ga.out_dtype = out_dtype;
+  ga.E = E;
+  ga.n_out = int(n_out);
+  ga.n_ext = int(n_ext);
+  ga.k_fwd = int(kc);
+  ga.ldo = ldo;
+  ga.err = err;
+  const int64_t stall = take_injected_stall();
+  ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
+  ga.stall_test = stall > 0 ? 1 : 0;
+  if (mode == MODE_FWD) {
+    grouped_gemm_kernel<MODE_FWD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
+    const int64_t row_bytes = n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
+    zero_tail_kernel<<<sms, 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), M, row_bytes);
+  } else {
+    grouped_gemm_kernel<MODE_WGRAD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace mxg
+
+using namespace mxg;
+
+extern "C" size_t mxg_grouped_fwd_workspace_size(int num_groups, int64_t m, int64_t n, int64_t k) {
+  if (num_groups < 1 || m < 0 || n < 0 || k < 0) return 0;
+  return ws_layout(MODE_FWD, num_groups, m, n, 0, k).total;
+}
+
+extern "C" size_t mxg_grouped_wgrad_workspace_size(int num_groups, int64_t m, int64_t n,
+                                                   int64_t k) {
+  if (num_groups < 1 || m < 0 || n < 0 || k < 0) return 0;
+  return ws_layout(MODE_WGRAD, num_groups, m, n, k, m).total;
+}
+
+static int check_common(int num_groups, int64_t m, int64_t n, int64_t k, int out_dtype,
+                        const int32_t* offs, int offs_len, int offs_kind) {
+  if (num_groups < 1) return MXG_ERR_INVALID_ARGUMENT;
+  if (num_groups > MXG_MAX_GROUPS) return MXG_ERR_TOO_MANY_GROUPS;
+  if (m < 0 || n < 1 || k < 1) return MXG_ERR_BAD_SHAPE;
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MXG_ERR_BAD_SHAPE;
+  if (out_dtype != MXG_DTYPE_BF16 && out_dtype != MXG_DTYPE_F32) return MXG_ERR_INVALID_ARGUMENT;
+  if (offs == nullptr) {
+    if (num_groups != 1) return MXG_ERR_INVALID_ARGUMENT;
+  } else {
+    if (offs_kind < MXG_OFFS_LEADING_ZERO || offs_kind > MXG_OFFS_AUTO) return MXG_ERR_INVALID_ARGUMENT;
+    const int need = offs_kind == MXG_OFFS_LEADING_ZERO ? num_groups + 1 : num_groups;
+    if (offs_kind == MXG_OFFS_AUTO) {
+      if (offs_len != num_groups && offs_len != num_groups + 1) return MXG_ERR_INVALID_ARGUMENT;
+    } else if (offs_len != need) {
+      return MXG_ERR_INVALID_ARGUMENT;
+    }
+  }
+  return MXG_OK;
+}
+
+extern "C" int mxg_grouped_fwd(const void* a, const void* a_scales, const void* w,
+                               const void* w_scales, const int32_t* offs, int offs_len,
+                               int offs_kind, int num_groups, int64_t m, int64_t n, int64_t k,
+                               void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  int st = check_common(num_groups, m, n, k, out_dtype, offs, offs_len, offs_kind);
+  if (st) return st;
+  if (k % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  if (m == 0) return MXG_OK;
+  if (!a || !w || !out || !workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(workspace))
+    return MXG_ERR_MISALIGNED;
+  if (int64_t(num_groups) * n > INT32_MAX) return MXG_ERR_BAD_SHAPE;
+  return launch_grouped(MODE_FWD, w, w_scales, int64_t(num_groups) * n, a, a_scales, m, k, offs,
+                        offs_len, offs_kind, num_groups, m, n, 0, out, out_dtype, n, workspace,
+                        workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_wgrad(const void* go, const void* go_scales, const void* ia,
+                                 const void* ia_scales, const int32_t* offs, int offs_len,
+                                 int offs_kind, int num_groups, int64_t m, int64_t n, int64_t k,
+                                 void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  int st = check_common(num_groups, m, n, k, out_dtype, offs, offs_len, offs_kind);
+  if (st) return st;
+  if (m % 32 != 0 || k % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (!go || !ia || !out || !workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(go) || !aligned16(ia) || !aligned16(out) || !aligned16(workspace))
+    return MXG_ERR_MISALIGNED;
+  if (m == 0) {  // no tokens: every dW[e] is zero
+    const size_t bytes = size_t(num_groups) * n * k * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
+    return cuda_status(cudaMemsetAsync(out, 0, bytes, (cudaStream_t)stream));
+  }
+  return launch_grouped(MODE_WGRAD, go, go_scales, n, ia, ia_scales, k, m, offs, offs_len,
+                        offs_kind, num_groups, m, n, k, out, out_dtype, k, workspace,
+                        workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" size_t mxg_dense_fwd_kn_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n < 0 || k < 0) return 0;
+  return align_up(size_t(n) * size_t(k), 1024) + ws_layout(MODE_FWD, 1, m, n, 0, k).total;
+}
+
+extern "C" int mxg_dense_fwd_kn(const void* x, const void* w_kn, int64_t m, int64_t n, int64_t k,
+                                void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  int st = check_common(1, m, n, k, out_dtype, nullptr, 0, 0);
+  if (st) return st;
+  if (k % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  if (m == 0) return MXG_OK;
+  if (!x || !w_kn || !out || !workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(out) || !aligned16(workspace)) return MXG_ERR_MISALIGNED;
+  if (workspace_bytes < mxg_dense_fwd_kn_workspace_size(m, n, k))
+    return MXG_ERR_WORKSPACE_TOO_SMALL;
+  // W [k, n] -> W^T [n, k] (K-contiguous rows for the MMA), then one group.
+  uint8_t* wt = reinterpret_cast<uint8_t*>(workspace);
+  const size_t wt_bytes = align_up(size_t(n) * size_t(k), 1024);
+  st = mxg_transpose_u8(w_kn, k, n, wt, stream);
+  if (st) return st;
+  return launch_grouped(MODE_FWD, wt, nullptr, n, x, nullptr, m, k, nullptr, 0, 0, 1, m, n, 0, out,
+                        out_dtype, n, wt + wt_bytes, workspace_bytes - wt_bytes,
+                        (cudaStream_t)stream);
+}

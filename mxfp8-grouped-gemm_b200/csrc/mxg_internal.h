@@ -1,0 +1,23 @@
+// Host-side helpers shared by the library's translation units.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "mxg.h"
+
+namespace mxg {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? MXG_OK : MXG_ERR_CUDA; }
+
+// Current device is an sm_100-class GPU (cached per device ordinal).
+int check_device();
+// SM count of the current device (cached).
+int num_sms();
+// Device address of the per-device error word (set up once per device).
+int* device_error_word();
+// Stall-injection limit armed by mxg_debug_inject_stall (consumed by the next launch).
+int64_t take_injected_stall();
+
+}  // namespace mxg

@@ -1,0 +1,227 @@
+// Inline-PTX helpers for sm_100a: mbarriers, TMA (no multicast), tcgen05
+// (TMEM alloc, block-scaled MMA, smem->TMEM copy, TMEM->register load) and
+// bounded waits that give up with an error status instead of hanging.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "mxg.h"
+
+namespace mxg {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Shared state for bounded waits inside one CTA: an abort flag any role can
+// raise and a per-wait time limit; every wait gives up once its limit passes
+// or the flag is set, so a lost arrival can never hang the GPU.
+struct WaitCtl {
+  volatile int* abort_flag;  // shared memory
+  int* err;                  // global error word (first error wins)
+  uint64_t limit_ns;         // longest a single wait may take
+};
+
+__device__ __forceinline__ void raise_error(const WaitCtl& w, int code) {
+  *w.abort_flag = 1;
+  atomicCAS(w.err, 0, code);
+}
+
+// Returns true when the phase with the given parity completed, false when the
+// wait gave up (limit passed -> MXG_ERR_DEVICE_TIMEOUT, or abort raised).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& w) {
+  uint32_t spins = 0;
+  uint64_t deadline = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0) {
+      if (*w.abort_flag) return false;
+      const uint64_t now = globaltimer_ns();
+      if (deadline == 0) {
+        deadline = now + w.limit_ns;
+      } else if (now > deadline) {
+        raise_error(w, MXG_ERR_DEVICE_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// A wait used only while unwinding after an abort: bounded, reports nothing.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  uint64_t end = globaltimer_ns() + limit_ns;
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() > end) return;
+  }
+}
+
+// ---------------------------------------------------------------- TMA / bulk
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// 2-D tiled load (no multicast) completing on an mbarrier's tx count.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Untiled bulk copy global->shared (16-byte aligned, size multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive on an mbarrier once every tcgen05 op issued so far by this thread
+// (MMAs, smem->TMEM copies) has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// 32 lanes x 128 bits from shared memory, replicated to all four TMEM lane
+// quarters (the scale-factor staging copy).
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// D(tmem) (+)= A(smem desc) x B(smem desc)^T with per-32-K E8M0 block scales
+// read from TMEM; kind::mxf8f6f4, one CTA.
+__device__ __forceinline__ void tc_mma_mxf8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread
+// (thread t of the warp holds TMEM lane (quarter*32 + t)).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor (sm_100 format): start >> 4 in [0,14),
+// leading byte offset >> 4 in [16,30), stride byte offset >> 4 in [32,46),
+// version 1 in [46,48), layout type in [61,64) (2 = 128-byte swizzle, 0 = none).
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                               uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7) << 61;
+  return d;
+}
+
+// K-major operand tile written by TMA with 128-byte swizzle: rows of 128
+// bytes, 8-row swizzle atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+  return make_sdesc(saddr, 16, 1024, 2);
+}
+
+// Scale-factor staging chunk: 32 rows x 16 bytes, no swizzle, 8-row core
+// matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sf_chunk(uint32_t saddr) {
+  return make_sdesc(saddr, 0, 128, 0);
+}
+
+// Instruction descriptor for kind::mxf8f6f4 block-scaled MMA, E4M3 x E4M3,
+// UE8M0 scales, both operands K-major: B format [10,13)=0, A format [7,10)=0,
+// N>>3 in [17,23), scale type UE8M0 bit 23, M>>4 in [24,29); the A/B
+// scale-factor byte selectors live in [29,31) and [4,6).
+__host__ __device__ __forceinline__ uint32_t make_idesc_mxf8(uint32_t m, uint32_t n) {
+  uint32_t d = 0;
+  d |= ((n >> 3) & 0x3F) << 17;
+  d |= 1u << 23;
+  d |= ((m >> 4) & 0x1F) << 24;
+  return d;
+}
+__device__ __forceinline__ uint32_t idesc_with_sf_id(uint32_t idesc, uint32_t a_id,
+                                                     uint32_t b_id) {
+  return idesc | ((a_id & 3) << 29) | ((b_id & 3) << 4);
+}
+
+}  // namespace mxg
