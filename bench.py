@@ -1,0 +1,537 @@
+"""Benchmark: MXFP8 grouped-GEMM TFLOPS (forward, wgrad) at DeepSeek-V3 shapes.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mxg|reference]
+
+One step (N=1, BASELINE configs 1 and 2, seeded synthetic data):
+  * gate/up forward   y_e = x_e . W_e^T   32 experts, K=7168, N=4096, bf16 out
+  * down-proj wgrad   dW_e = dy_e^T . h_e  N=7168, K=2048, fp32 out
+  * gate/up wgrad     dW_e = dy_e^T . x_e  N=4096, K=7168, fp32 out
+over 65536 routed rows split by a seeded multinomial over Dirichlet(1.0)
+expert probabilities, groups padded to 32.  Operands are MXFP8 (e4m3 + E8M0,
+quantised before timing; weights are static).  Each GEMM is one full call of
+the reference-facing API (group scheduler + scale packing + tensor-core
+kernel).  ``value`` = algorithmic FLOPs (2 * real rows * N * K) / time.
+All operands together exceed the 126 MB L2, so no explicit flush is needed.
+
+N>1 (torchrun, one rank per GPU): every rank runs the same per-GPU workload
+(weak scaling); the step time is the max over ranks.
+
+``--impl reference`` times the reference's CPU path (torch dequantise + fp32
+matmul, restated in oracle/) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MXFP8 grouped-GEMM TFLOPS (fwd, wgrad) at DSv3 shapes; % of FP8 TC peak"
+E, HIDDEN, INTER, GATE_UP = 32, 7168, 2048, 4096
+ROUTED_ROWS = 65536
+
+
+def pkg():
+    return importlib.import_module("mxfp8-grouped-gemm_b200")
+
+
+# ---------------------------------------------------------------- distributed
+def dist_init(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- peaks / clocks
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"fp8_tflops": 2.0 * p["bf16_tflops_sustained"],
+                "fp8_tflops_burst": 2.0 * p["bf16_tflops"],
+                "hbm_gbs": p["hbm_gbs"],
+                "source": "2 x measured cuBLAS bf16 (MEASURED_PEAKS.json has no fp8 entry); "
+                          "sustained figure (kernels timed inside a long step)"}
+    return {"fp8_tflops": 2.0 * 1400.0, "fp8_tflops_burst": 2.0 * 1590.0, "hbm_gbs": 6650.0,
+            "source": "fallback: 2 x 1.4 PFLOP/s sustained bf16, 6.65 TB/s"}
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- workload
+class Workload:
+    """Device-resident MXFP8 operands of the DSv3 GEMM set."""
+
+    def __init__(self, seed=0, device="cuda", experts=None, rows=None):
+        m = pkg()
+        W = m.workloads
+        global E
+        E = experts or E
+        self.split = W.dirichlet_split(rows or ROUTED_ROWS, E, 1.0, seed=seed)
+        sp = self.split
+        self.M = sp.M
+        dev = torch.device(device)
+        self.offs = torch.from_numpy(sp.offs_cumulative()).to(dev)
+        self.sizes = torch.from_numpy(sp.padded.astype(np.int32)).to(dev)
+        x = W.routed_activations(sp, HIDDEN, 1.0, dev, seed + 10)
+        h = W.routed_activations(sp, INTER, 1.0, dev, seed + 11)
+        dy_down = W.routed_activations(sp, HIDDEN, 1e-2, dev, seed + 12)
+        dy_gu = W.routed_activations(sp, GATE_UP, 1e-2, dev, seed + 13)
+        w_gu = W.expert_weights(E, GATE_UP, HIDDEN, 0.02, dev, seed + 14)
+        self.bf16 = {"x": x, "h": h, "dy_down": dy_down, "dy_gu": dy_gu}
+        self.xq, self.xs = m.quantize_rowwise(x)
+        wq, ws = m.quantize_rowwise(w_gu.view(E * GATE_UP, HIDDEN))
+        self.wq, self.ws = wq.view(E, GATE_UP, HIDDEN), ws.view(E, GATE_UP, HIDDEN // 32)
+        del w_gu
+        self.go_d, self.gos_d = m.quantize_colwise(dy_down)   # [7168, M]
+        self.ia_d, self.ias_d = m.quantize_colwise(h)         # [2048, M]
+        self.go_g, self.gos_g = m.quantize_colwise(dy_gu)     # [4096, M]
+        self.ia_g, self.ias_g = m.quantize_colwise(x)         # [7168, M]
+        self.y = torch.empty(self.M, GATE_UP, dtype=torch.bfloat16, device=dev)
+        self.dw_d = torch.empty(E, HIDDEN, INTER, dtype=torch.float32, device=dev)
+        self.dw_g = torch.empty(E, GATE_UP, HIDDEN, dtype=torch.float32, device=dev)
+        rows = sp.real_rows
+        self.flops = {"fwd_gate_up": 2 * rows * GATE_UP * HIDDEN,
+                      "wgrad_down": 2 * rows * HIDDEN * INTER,
+                      "wgrad_gate_up": 2 * rows * GATE_UP * HIDDEN}
+        torch.cuda.synchronize()
+
+    def gemm_calls(self):
+        """The three API calls of one step, each as (name, prepare, run)."""
+        m = pkg()
+        ops = m.ops
+        L = m._lib.load()
+        s = lambda: m._lib.stream_ptr()
+        ws_f = m._lib.workspace(L.mxg_grouped_fwd_workspace_size(E, self.M, GATE_UP, HIDDEN), self.y.device)
+        self._ws = {"f": ws_f}
+        ws_d = torch.empty(L.mxg_grouped_wgrad_workspace_size(E, self.M, HIDDEN, INTER), dtype=torch.uint8, device=self.y.device)
+        ws_g = torch.empty(L.mxg_grouped_wgrad_workspace_size(E, self.M, GATE_UP, HIDDEN), dtype=torch.uint8, device=self.y.device)
+        self._ws.update(d=ws_d, g=ws_g)
+        chk = m._lib.check
+        M = self.M
+
+        def fwd_prep():
+            chk(L.mxg_grouped_fwd_prepare(self.xs.data_ptr(), self.ws.data_ptr(), self.offs.data_ptr(),
+                                          E, 1, E, M, GATE_UP, HIDDEN, ws_f.data_ptr(), ws_f.numel(), s()), "prep")
+
+        def fwd_run():
+            chk(L.mxg_grouped_fwd_run(self.xq.data_ptr(), self.wq.data_ptr(), E, M, GATE_UP, HIDDEN,
+                                      self.y.data_ptr(), 0, ws_f.data_ptr(), ws_f.numel(), s()), "run")
+
+        def wd_prep():
+            chk(L.mxg_grouped_wgrad_prepare(self.gos_d.data_ptr(), self.ias_d.data_ptr(), self.sizes.data_ptr(),
+                                            E, 2, E, M, HIDDEN, INTER, ws_d.data_ptr(), ws_d.numel(), s()), "prep")
+
+        def wd_run():
+            chk(L.mxg_grouped_wgrad_run(self.go_d.data_ptr(), self.ia_d.data_ptr(), E, M, HIDDEN, INTER,
+                                        self.dw_d.data_ptr(), 1, ws_d.data_ptr(), ws_d.numel(), s()), "run")
+
+        def wg_prep():
+            chk(L.mxg_grouped_wgrad_prepare(self.gos_g.data_ptr(), self.ias_g.data_ptr(), self.sizes.data_ptr(),
+                                            E, 2, E, M, GATE_UP, HIDDEN, ws_g.data_ptr(), ws_g.numel(), s()), "prep")
+
+        def wg_run():
+            chk(L.mxg_grouped_wgrad_run(self.go_g.data_ptr(), self.ia_g.data_ptr(), E, M, GATE_UP, HIDDEN,
+                                        self.dw_g.data_ptr(), 1, ws_g.data_ptr(), ws_g.numel(), s()), "run")
+
+        return [("fwd_gate_up", fwd_prep, fwd_run), ("wgrad_down", wd_prep, wd_run),
+                ("wgrad_gate_up", wg_prep, wg_run)]
+
+    def quantize_step(self):
+        """The activation quantisations one training step needs (weights are static)."""
+        m = pkg()
+        m.quantize_rowwise(self.bf16["x"])
+        m.quantize_colwise(self.bf16["x"])
+        m.quantize_colwise(self.bf16["h"])
+        m.quantize_colwise(self.bf16["dy_down"])
+        m.quantize_colwise(self.bf16["dy_gu"])
+
+    def quantize_bytes(self):
+        tot = 0
+        for name, t in self.bf16.items():
+            n = t.numel()
+            reps = 2 if name == "x" else 1
+            tot += reps * (2 * n + n + n // 32)
+        return tot
+
+
+LAUNCHES_PER_CALL = {"fwd_gate_up": 5, "wgrad_down": 4, "wgrad_gate_up": 4}  # our kernels per API call
+
+
+def time_steps(calls, steps, warmup, world):
+    """Events around every prepare/run of every step; returns per-step total
+    ms and per-call run-kernel ms (averages)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        for _, prep, run in calls:
+            prep()
+            run()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * len(calls) + 1)] for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        e = ev[i]
+        e[0].record(stream)
+        for j, (_, prep, run) in enumerate(calls):
+            prep()
+            e[2 * j + 1].record(stream)
+            run()
+            e[2 * j + 2].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    total_ms = start.elapsed_time(end)
+    run_ms = {name: 0.0 for name, _, _ in calls}
+    prep_ms = {name: 0.0 for name, _, _ in calls}
+    for e in ev:
+        for j, (name, _, _) in enumerate(calls):
+            prep_ms[name] += e[2 * j].elapsed_time(e[2 * j + 1])
+            run_ms[name] += e[2 * j + 1].elapsed_time(e[2 * j + 2])
+    return total_ms / steps, {k: v / steps for k, v in run_ms.items()}, {k: v / steps for k, v in prep_ms.items()}
+
+
+def e2e_measure(wl, steps):
+    """Host-buffer end to end through the public API: pinned host operands ->
+    H2D -> fused_grouped_fwd / wgrad_fused -> D2H of the results."""
+    m = pkg()
+    dev = wl.y.device
+    host = {}
+    for name in ("xq", "xs", "wq", "ws", "offs", "go_d", "gos_d", "ia_d", "ias_d", "go_g", "gos_g",
+                 "ia_g", "ias_g", "sizes"):
+        t = getattr(wl, name)
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        host[name] = h
+    y_h = torch.empty(wl.y.shape, dtype=wl.y.dtype, pin_memory=True)
+    dwd_h = torch.empty(wl.dw_d.shape, dtype=wl.dw_d.dtype, pin_memory=True)
+    dwg_h = torch.empty(wl.dw_g.shape, dtype=wl.dw_g.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in (y_h, dwd_h, dwg_h))
+
+    def step():
+        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        y = m.fused_grouped_fwd(d["xq"], d["wq"], d["offs"], d["xs"], d["ws"])
+        dwd = m.wgrad_fused(d["go_d"], d["ia_d"], d["sizes"], d["gos_d"], d["ias_d"], out_dtype=torch.float32)
+        dwg = m.wgrad_fused(d["go_g"], d["ia_g"], d["sizes"], d["gos_g"], d["ias_g"], out_dtype=torch.float32)
+        y_h.copy_(y, non_blocking=True)
+        dwd_h.copy_(dwd, non_blocking=True)
+        dwg_h.copy_(dwg, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    return ms, h2d, d2h
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_reference_sample(wl_cpu, experts, threads):
+    """The reference's torch path on the host: dequantise (q * 2^(s-127)) in
+    fp32 and per-expert fp32 matmul, for the given experts of each GEMM."""
+    from oracle import mxfp8_oracle as orc
+    torch.set_num_threads(threads)
+    flops = 0
+    t0 = time.perf_counter()
+    for e in experts:
+        s, t = wl_cpu["starts"][e], wl_cpu["ends"][e]
+        if t <= s:
+            continue
+        a = orc.dequantize_torch(wl_cpu["xq"][s:t], wl_cpu["xs"][s:t])
+        w = orc.dequantize_torch(wl_cpu["wq"][e], wl_cpu["ws"][e])
+        _ = a @ w.T
+        go = orc.dequantize_torch(wl_cpu["go_d"][:, s:t], wl_cpu["gos_d"][:, s // 32:t // 32])
+        ia = orc.dequantize_torch(wl_cpu["ia_d"][:, s:t], wl_cpu["ias_d"][:, s // 32:t // 32])
+        _ = go @ ia.T
+        go = orc.dequantize_torch(wl_cpu["go_g"][:, s:t], wl_cpu["gos_g"][:, s // 32:t // 32])
+        ia = orc.dequantize_torch(wl_cpu["ia_g"][:, s:t], wl_cpu["ias_g"][:, s // 32:t // 32])
+        _ = go @ ia.T
+        real = int(wl_cpu["real"][e])
+        flops += 2 * real * (GATE_UP * HIDDEN + HIDDEN * INTER + GATE_UP * HIDDEN)
+    dt = time.perf_counter() - t0
+    return flops, dt
+
+
+def cpu_copy_of(wl, experts):
+    """Host copies of the operand slices the CPU sample touches."""
+    sp = wl.split
+    ends = np.cumsum(sp.padded)
+    starts = ends - sp.padded
+    lo = int(min(starts[e] for e in experts))
+    hi = int(max(ends[e] for e in experts))
+    d = {"starts": {e: int(starts[e]) - lo for e in experts}, "ends": {e: int(ends[e]) - lo for e in experts},
+         "real": sp.real}
+    d["xq"] = wl.xq[lo:hi].view(torch.uint8).cpu()
+    d["xs"] = wl.xs[lo:hi].cpu()
+    d["wq"] = {e: wl.wq[e].view(torch.uint8).cpu() for e in experts}
+    d["ws"] = {e: wl.ws[e].cpu() for e in experts}
+    for k in ("go_d", "ia_d", "go_g", "ia_g"):
+        d[k] = getattr(wl, k)[:, lo:hi].view(torch.uint8).cpu()
+    for k in ("gos_d", "ias_d", "gos_g", "ias_g"):
+        d[k] = getattr(wl, k)[:, lo // 32:hi // 32].cpu()
+    return d
+
+
+def sample_experts(wl, n=2):
+    """The n median-sized experts (a representative, bounded CPU sample)."""
+    order = np.argsort(wl.split.real)
+    mid = len(order) // 2
+    return sorted(int(i) for i in order[mid - n // 2: mid - n // 2 + n])
+
+
+# ---------------------------------------------------------------- arms
+def traffic_from_profiles():
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        try:
+            return json.load(open(path))
+        except Exception:
+            return {}
+    return {}
+
+
+def run_mxg(args, rank, world, local):
+    m = pkg()
+    m._lib.load()
+    if args.case == "small":
+        # reduced problem for profiler captures: 8 experts, 16384 routed rows
+        # (operands ~0.6 GB, still larger than L2)
+        wl = Workload(seed=args.seed, experts=8, rows=16384)
+    else:
+        wl = Workload(seed=args.seed)
+    calls = wl.gemm_calls()
+    pk = peaks()
+    with ClockSampler(local) as clk:
+        ms_step, run_ms, prep_ms = time_steps(calls, args.steps, args.warmup, world)
+    code = m.device_error()
+    if code:
+        raise RuntimeError(f"device error {code} during the timed region")
+    ms_step = max_over_ranks(ms_step, world)
+    flops_step = sum(wl.flops.values())
+    value = world * flops_step / (ms_step * 1e-3) / 1e12
+    per = {}
+    for name in run_ms:
+        per[name] = {"tflops_kernel": wl.flops[name] / (run_ms[name] * 1e-3) / 1e12,
+                     "kernel_ms": run_ms[name], "prepare_ms": prep_ms[name],
+                     "tflops_call": wl.flops[name] / ((run_ms[name] + prep_ms[name]) * 1e-3) / 1e12}
+    dom = max(run_ms, key=lambda k: run_ms[k])
+    traffic = traffic_from_profiles().get(dom)
+    achieved = wl.flops[dom] / (run_ms[dom] * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": f"grouped_gemm_kernel ({dom})",
+                "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1),
+                "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
+                "frac_of_burst_peak": round(achieved / pk["fp8_tflops_burst"], 4),
+                "peak_source": pk["source"], "traffic": traffic,
+                "flops_per_launch": wl.flops[dom], "per_kernel": per}
+    # quantiser throughput (separate timed loop, HBM bound)
+    torch.cuda.synchronize()
+    qs, qe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        wl.quantize_step()
+    qs.record()
+    qreps = 10
+    for _ in range(qreps):
+        wl.quantize_step()
+    qe.record()
+    torch.cuda.synchronize()
+    q_ms = qs.elapsed_time(qe) / qreps
+    quant = {"ms_per_step": q_ms, "gbs": wl.quantize_bytes() / (q_ms * 1e-3) / 1e9,
+             "frac_hbm": wl.quantize_bytes() / (q_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+             "tflops_gemms_incl_quantize": world * flops_step / ((ms_step + q_ms) * 1e-3) / 1e12}
+    e2e = None
+    if not args.no_e2e:
+        e2e_ms, h2d, d2h = e2e_measure(wl, max(2, min(5, args.steps)))
+        e2e_ms = max_over_ranks(e2e_ms, world)
+        e2e = {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        experts = sample_experts(wl, 2)
+        host = cpu_copy_of(wl, experts)
+        threads = os.cpu_count() or 1
+        cpu_reference_sample(host, experts[:1], threads)  # warm-up
+        fl, dt = cpu_reference_sample(host, experts, threads)
+        cpu = {"value": round(fl / dt / 1e12, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"experts {experts} of the step (their fwd gate/up + both wgrads, "
+                         f"{fl / 1e12:.2f} TFLOP), torch fp32 dequantise+matmul on the host"}
+    out = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
+           "data": "synthetic",
+           "config": {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)"
+                      if args.case == "dsv3" else "small profiling case (8 experts, 16384 rows)",
+                      "experts_per_gpu": E, "hidden": HIDDEN, "intermediate": INTER,
+                      "routed_rows_per_gpu": wl.split.real_rows, "padded_rows": wl.M,
+                      "routing": "multinomial over Dirichlet(1.0), groups padded to 32",
+                      "flops_per_step_per_gpu": flops_step, "l2": "operands > L2 (no flush needed)",
+                      "parallelism": f"ep{world}" if world > 1 else "single"},
+           "roofline": roofline, "quantize": quant, "cpu_baseline": cpu, "e2e": e2e,
+           "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.values()),
+           "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def run_reference(args, rank, world, local):
+    """Reference arm: the reference's CPU torch path, rank 0 only."""
+    if rank != 0:
+        return
+    m = pkg()
+    from oracle import mxfp8_oracle as orc  # noqa: F401  (the checker, used as the timed CPU port)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # The same seeded operands, produced on the host (no GPU needed for this arm).
+    sp = m.workloads.dirichlet_split(ROUTED_ROWS, E, 1.0, seed=args.seed)
+    experts = [int(i) for i in np.argsort(sp.real)[len(sp.real) // 2 - 1: len(sp.real) // 2 + 1]]
+    g = torch.Generator().manual_seed(args.seed)
+    host = {"starts": {}, "ends": {}, "real": sp.real, "wq": {}, "ws": {}}
+    rows = int(sum(sp.padded[e] for e in experts))
+    rnd = lambda *s: torch.randint(0, 126, s, generator=g, dtype=torch.uint8)
+    sc = lambda *s: torch.randint(118, 128, s, generator=g, dtype=torch.uint8)
+    off = 0
+    for e in experts:
+        host["starts"][e], host["ends"][e] = off, off + int(sp.padded[e])
+        off += int(sp.padded[e])
+        host["wq"][e], host["ws"][e] = rnd(GATE_UP, HIDDEN), sc(GATE_UP, HIDDEN // 32)
+    host["xq"], host["xs"] = rnd(rows, HIDDEN), sc(rows, HIDDEN // 32)
+    host["go_d"], host["gos_d"] = rnd(HIDDEN, rows), sc(HIDDEN, rows // 32)
+    host["ia_d"], host["ias_d"] = rnd(INTER, rows), sc(INTER, rows // 32)
+    host["go_g"], host["gos_g"] = rnd(GATE_UP, rows), sc(GATE_UP, rows // 32)
+    host["ia_g"], host["ias_g"] = rnd(HIDDEN, rows), sc(HIDDEN, rows // 32)
+    for _ in range(args.warmup):
+        cpu_reference_sample(host, experts, threads)
+    tot_fl, tot_dt = 0, 0.0
+    for _ in range(args.steps):
+        fl, dt = cpu_reference_sample(host, experts, threads)
+        tot_fl += fl
+        tot_dt += dt
+    v = tot_fl / tot_dt / 1e12
+    out = {"metric": METRIC, "value": round(v, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(1e3 * tot_dt / args.steps, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic", "impl": "reference",
+           "config": {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)",
+                      "experts_per_gpu": E, "hidden": HIDDEN, "intermediate": INTER},
+           "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
+                            "kind": "port",
+                            "sample": f"per step experts {experts} (their fwd gate/up + both wgrads), "
+                                      "torch fp32 dequantise+matmul (reference fused_fwd.py:249-264, "
+                                      "scale_correctness.py:110-137)"},
+           "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mxg", choices=["mxg", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--case", default="dsv3", choices=["dsv3", "small"],
+                    help="small: reduced problem for profiler captures (not a bench line)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")), 0)
+        return
+    rank, world, local = dist_init(args.gpus)
+    try:
+        run_mxg(args, rank, world, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -101,6 +101,19 @@ MXG_API int mxg_grouped_fwd(const void* a, const void* a_scales, const void* w, 
                     int64_t n, int64_t k, void* out, int out_dtype, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Two-phase form of mxg_grouped_fwd (same workspace, same stream order):
+ * prepare reads offs and the scales (group scheduler + scale-factor packing
+ * into the workspace), run launches the tensor-core kernel on the e4m3
+ * operands with the groups and scales captured by the last prepare on that
+ * workspace.  prepare + run == mxg_grouped_fwd. */
+MXG_API int mxg_grouped_fwd_prepare(const void* a_scales, const void* w_scales, const int32_t* offs,
+                                    int offs_len, int offs_kind, int num_groups, int64_t m,
+                                    int64_t n, int64_t k, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+MXG_API int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups, int64_t m, int64_t n,
+                                int64_t k, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* ---- dense forward with a K x N weight: out[m, n] = x[m, k] . w[k, n] -------
  * Unit scales (the reference's fwd_ge passes none, fwd_final.py:101-106).
  * Replaces fwd_final.py:121-131 fwd_ge. */
@@ -121,6 +134,17 @@ MXG_API int mxg_grouped_wgrad(const void* go, const void* go_scales, const void*
                       const void* ia_scales, const int32_t* offs, int offs_len, int offs_kind,
                       int num_groups, int64_t m, int64_t n, int64_t k, void* out, int out_dtype,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Two-phase form of mxg_grouped_wgrad, the counterpart of the reference's
+ * wgrad_prepare()/wgrad_kernel() split (wgrad_fused.py:74-112), without its
+ * operand copies: prepare reads offs and the scales, run the e4m3 operands. */
+MXG_API int mxg_grouped_wgrad_prepare(const void* go_scales, const void* ia_scales,
+                                      const int32_t* offs, int offs_len, int offs_kind,
+                                      int num_groups, int64_t m, int64_t n, int64_t k,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+MXG_API int mxg_grouped_wgrad_run(const void* go, const void* ia, int num_groups, int64_t m,
+                                  int64_t n, int64_t k, void* out, int out_dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /* ---- byte transpose: dst [cols, rows] = src [rows, cols]^T (uint8) ----------- */
 MXG_API int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, void* dst, void* stream);

@@ -35,6 +35,14 @@ _PROTOS = {
     "mxg_grouped_fwd_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64]),
     "mxg_grouped_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
                                  _c_i64, _vp, _c_int, _vp, _c_size, _vp]),
+    "mxg_grouped_fwd_prepare": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
+                                         _c_i64, _vp, _c_size, _vp]),
+    "mxg_grouped_fwd_run": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,
+                                     _c_size, _vp]),
+    "mxg_grouped_wgrad_prepare": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
+                                           _c_i64, _vp, _c_size, _vp]),
+    "mxg_grouped_wgrad_run": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,
+                                       _c_size, _vp]),
     "mxg_dense_fwd_kn_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "mxg_dense_fwd_kn": (_c_int, [_vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp, _c_size, _vp]),
     "mxg_grouped_wgrad_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64]),

@@ -711,15 +711,49 @@ static int configure_kernels() {
 
 static constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per wait
 
-// Shared launcher for both modes.
-//   A operand: a_ptr [a_rows, kc] e4m3, scales a_sc [a_rows, kc/32]
-//   B operand: b_ptr [b_rows, kc] e4m3, scales b_sc [b_rows, kc/32]
-static int launch_grouped(int mode, const void* a_ptr, const void* a_sc, int64_t a_rows,
-                          const void* b_ptr, const void* b_sc, int64_t b_rows, int64_t kc,
-                          const int32_t* offs, int offs_len, int offs_kind, int E, int64_t M,
-                          int64_t n_out, int64_t n_ext, void* out, int out_dtype, int64_t ldo,
-                          void* ws, size_t ws_bytes, cudaStream_t stream) {
-  const WsLayout L = ws_layout(mode, E, M, n_out, n_ext, kc);
+// Host launch is split in two halves that share the workspace:
+//   prepare: group scheduler + scale-factor packing (reads offs and scales)
+//   run:     the tcgen05 GEMM kernel (reads the e4m3 operands)
+// A operand: rows of [a_rows, kc] e4m3; B operand: rows of [b_rows, kc] e4m3.
+struct Problem {
+  int mode;
+  int E;
+  int64_t M;      // rows covered by offs (forward: tokens; wgrad: tokens)
+  int64_t n_out;  // A rows per group
+  int64_t n_ext;  // wgrad: B rows
+  int64_t kc;     // contraction length (forward K; wgrad M)
+};
+
+static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
+                           const int32_t* offs, int offs_len, int offs_kind, void* ws,
+                           size_t ws_bytes, cudaStream_t stream) {
+  const WsLayout L = ws_layout(P.mode, P.E, P.M, P.n_out, P.n_ext, P.kc);
+  if (ws_bytes < L.total) return MXG_ERR_WORKSPACE_TOO_SMALL;
+  int st = check_device();
+  if (st) return st;
+  uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+  int* meta = reinterpret_cast<int*>(wsb + L.meta_off);
+  int* err = device_error_word();
+  if (!err) return MXG_ERR_CUDA;
+  SchedArgs sa{offs, offs_len, offs_kind, P.E, int(P.M), P.mode, int(P.n_out), int(P.n_ext),
+               int(P.kc), meta, err};
+  schedule_kernel<<<1, MXG_MAX_GROUPS, 0, stream>>>(sa);
+  const int sms = num_sms();
+  PackArgs pa{meta, P.E, P.mode, 0, reinterpret_cast<const uint8_t*>(a_sc), P.kc / 32,
+              wsb + L.sfa_off, int(P.n_out), int(P.n_ext), int(P.kc)};
+  pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pa);
+  PackArgs pb = pa;
+  pb.side = 1;
+  pb.src = reinterpret_cast<const uint8_t*>(b_sc);
+  pb.dst = wsb + L.sfb_off;
+  pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+  return cuda_status(cudaGetLastError());
+}
+
+static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, const void* b_ptr,
+                       int64_t b_rows, void* out, int out_dtype, int64_t ldo, void* ws,
+                       size_t ws_bytes, cudaStream_t stream) {
+  const WsLayout L = ws_layout(P.mode, P.E, P.M, P.n_out, P.n_ext, P.kc);
   if (ws_bytes < L.total) return MXG_ERR_WORKSPACE_TOO_SMALL;
   int st = check_device();
   if (st) return st;
@@ -727,49 +761,34 @@ static int launch_grouped(int mode, const void* a_ptr, const void* a_sc, int64_t
   if (st) return st;
   uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
   int* meta = reinterpret_cast<int*>(wsb + L.meta_off);
-  uint8_t* sfa = wsb + L.sfa_off;
-  uint8_t* sfb = wsb + L.sfb_off;
   int* err = device_error_word();
   if (!err) return MXG_ERR_CUDA;
-
   CUtensorMap tmA, tmB;
-  st = make_tmap(&tmA, a_ptr, a_rows, kc, kBM);
+  st = make_tmap(&tmA, a_ptr, a_rows, P.kc, kBM);
   if (st) return st;
-  st = make_tmap(&tmB, b_ptr, b_rows, kc, kBNMax);
+  st = make_tmap(&tmB, b_ptr, b_rows, P.kc, kBNMax);
   if (st) return st;
-
-  SchedArgs sa{offs, offs_len, offs_kind, E, int(M), mode, int(n_out), int(n_ext), int(kc), meta, err};
-  schedule_kernel<<<1, MXG_MAX_GROUPS, 0, stream>>>(sa);
-
-  const int sms = num_sms();
-  PackArgs pa{meta, E, mode, 0, reinterpret_cast<const uint8_t*>(a_sc), kc / 32, sfa,
-              int(n_out), int(n_ext), int(kc)};
-  pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pa);
-  PackArgs pb = pa;
-  pb.side = 1;
-  pb.src = reinterpret_cast<const uint8_t*>(b_sc);
-  pb.dst = sfb;
-  pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
-
   GemmArgs ga;
   ga.meta = meta;
-  ga.sfa_pack = sfa;
-  ga.sfb_pack = sfb;
+  ga.sfa_pack = wsb + L.sfa_off;
+  ga.sfb_pack = wsb + L.sfb_off;
   ga.out = out;
   ga.out_dtype = out_dtype;
-  ga.E = E;
-  ga.n_out = int(n_out);
-  ga.n_ext = int(n_ext);
-  ga.k_fwd = int(kc);
+  ga.E = P.E;
+  ga.n_out = int(P.n_out);
+  ga.n_ext = int(P.n_ext);
+  ga.k_fwd = int(P.kc);
   ga.ldo = ldo;
   ga.err = err;
   const int64_t stall = take_injected_stall();
   ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
   ga.stall_test = stall > 0 ? 1 : 0;
-  if (mode == MODE_FWD) {
+  const int sms = num_sms();
+  if (P.mode == MODE_FWD) {
     grouped_gemm_kernel<MODE_FWD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
-    const int64_t row_bytes = n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
-    zero_tail_kernel<<<sms, 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), M, row_bytes);
+    const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
+    zero_tail_kernel<<<sms, 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
+                                               row_bytes);
   } else {
     grouped_gemm_kernel<MODE_WGRAD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
   }
@@ -790,6 +809,9 @@ extern "C" size_t mxg_grouped_wgrad_workspace_size(int num_groups, int64_t m, in
   if (num_groups < 1 || m < 0 || n < 0 || k < 0) return 0;
   return ws_layout(MODE_WGRAD, num_groups, m, n, k, m).total;
 }
+
+// Stand-in offs pointer for validating run() arguments; never dereferenced.
+static const int32_t* const kOffsGivenToPrepare = reinterpret_cast<const int32_t*>(uintptr_t(16));
 
 static int check_common(int num_groups, int64_t m, int64_t n, int64_t k, int out_dtype,
                         const int32_t* offs, int offs_len, int offs_kind) {
@@ -825,9 +847,46 @@ extern "C" int mxg_grouped_fwd(const void* a, const void* a_scales, const void* 
   if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(workspace))
     return MXG_ERR_MISALIGNED;
   if (int64_t(num_groups) * n > INT32_MAX) return MXG_ERR_BAD_SHAPE;
-  return launch_grouped(MODE_FWD, w, w_scales, int64_t(num_groups) * n, a, a_scales, m, k, offs,
-                        offs_len, offs_kind, num_groups, m, n, 0, out, out_dtype, n, workspace,
-                        workspace_bytes, (cudaStream_t)stream);
+  const Problem P{MODE_FWD, num_groups, m, n, 0, k};
+  st = prepare_grouped(P, w_scales, a_scales, offs, offs_len, offs_kind, workspace,
+                       workspace_bytes, (cudaStream_t)stream);
+  if (st) return st;
+  return run_grouped(P, w, int64_t(num_groups) * n, a, m, out, out_dtype, n, workspace,
+                     workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_fwd_prepare(const void* a_scales, const void* w_scales,
+                                       const int32_t* offs, int offs_len, int offs_kind,
+                                       int num_groups, int64_t m, int64_t n, int64_t k,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_common(num_groups, m, n, k, MXG_DTYPE_BF16, offs, offs_len, offs_kind);
+  if (st) return st;
+  if (k % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  if (!workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(workspace)) return MXG_ERR_MISALIGNED;
+  if (m == 0) return MXG_OK;
+  if (int64_t(num_groups) * n > INT32_MAX) return MXG_ERR_BAD_SHAPE;
+  const Problem P{MODE_FWD, num_groups, m, n, 0, k};
+  return prepare_grouped(P, w_scales, a_scales, offs, offs_len, offs_kind, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups, int64_t m,
+                                   int64_t n, int64_t k, void* out, int out_dtype,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  // offs were captured by prepare; validate the rest as if they were present
+  int st = check_common(num_groups, m, n, k, out_dtype, kOffsGivenToPrepare, num_groups,
+                        MXG_OFFS_SIZES);
+  if (st) return st;
+  if (k % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  if (m == 0) return MXG_OK;
+  if (!a || !w || !out || !workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(out) || !aligned16(workspace))
+    return MXG_ERR_MISALIGNED;
+  if (int64_t(num_groups) * n > INT32_MAX) return MXG_ERR_BAD_SHAPE;
+  const Problem P{MODE_FWD, num_groups, m, n, 0, k};
+  return run_grouped(P, w, int64_t(num_groups) * n, a, m, out, out_dtype, n, workspace,
+                     workspace_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int mxg_grouped_wgrad(const void* go, const void* go_scales, const void* ia,
@@ -845,9 +904,47 @@ extern "C" int mxg_grouped_wgrad(const void* go, const void* go_scales, const vo
     const size_t bytes = size_t(num_groups) * n * k * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
     return cuda_status(cudaMemsetAsync(out, 0, bytes, (cudaStream_t)stream));
   }
-  return launch_grouped(MODE_WGRAD, go, go_scales, n, ia, ia_scales, k, m, offs, offs_len,
-                        offs_kind, num_groups, m, n, k, out, out_dtype, k, workspace,
-                        workspace_bytes, (cudaStream_t)stream);
+  const Problem P{MODE_WGRAD, num_groups, m, n, k, m};
+  st = prepare_grouped(P, go_scales, ia_scales, offs, offs_len, offs_kind, workspace,
+                       workspace_bytes, (cudaStream_t)stream);
+  if (st) return st;
+  return run_grouped(P, go, n, ia, k, out, out_dtype, k, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_wgrad_prepare(const void* go_scales, const void* ia_scales,
+                                         const int32_t* offs, int offs_len, int offs_kind,
+                                         int num_groups, int64_t m, int64_t n, int64_t k,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_common(num_groups, m, n, k, MXG_DTYPE_BF16, offs, offs_len, offs_kind);
+  if (st) return st;
+  if (m % 32 != 0 || k % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (!workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(workspace)) return MXG_ERR_MISALIGNED;
+  if (m == 0) return MXG_OK;
+  const Problem P{MODE_WGRAD, num_groups, m, n, k, m};
+  return prepare_grouped(P, go_scales, ia_scales, offs, offs_len, offs_kind, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_wgrad_run(const void* go, const void* ia, int num_groups, int64_t m,
+                                     int64_t n, int64_t k, void* out, int out_dtype,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  // offs were captured by prepare; validate the rest as if they were present
+  int st = check_common(num_groups, m, n, k, out_dtype, kOffsGivenToPrepare, num_groups,
+                        MXG_OFFS_SIZES);
+  if (st) return st;
+  if (m % 32 != 0 || k % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (!go || !ia || !out || !workspace) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(go) || !aligned16(ia) || !aligned16(out) || !aligned16(workspace))
+    return MXG_ERR_MISALIGNED;
+  if (m == 0) {
+    const size_t bytes = size_t(num_groups) * n * k * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
+    return cuda_status(cudaMemsetAsync(out, 0, bytes, (cudaStream_t)stream));
+  }
+  const Problem P{MODE_WGRAD, num_groups, m, n, k, m};
+  return run_grouped(P, go, n, ia, k, out, out_dtype, k, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
 }
 
 extern "C" size_t mxg_dense_fwd_kn_workspace_size(int64_t m, int64_t n, int64_t k) {
@@ -871,7 +968,10 @@ extern "C" int mxg_dense_fwd_kn(const void* x, const void* w_kn, int64_t m, int6
   const size_t wt_bytes = align_up(size_t(n) * size_t(k), 1024);
   st = mxg_transpose_u8(w_kn, k, n, wt, stream);
   if (st) return st;
-  return launch_grouped(MODE_FWD, wt, nullptr, n, x, nullptr, m, k, nullptr, 0, 0, 1, m, n, 0, out,
-                        out_dtype, n, wt + wt_bytes, workspace_bytes - wt_bytes,
-                        (cudaStream_t)stream);
+  const Problem P{MODE_FWD, 1, m, n, 0, k};
+  st = prepare_grouped(P, nullptr, nullptr, nullptr, 0, 0, wt + wt_bytes,
+                       workspace_bytes - wt_bytes, (cudaStream_t)stream);
+  if (st) return st;
+  return run_grouped(P, wt, n, x, m, out, out_dtype, n, wt + wt_bytes, workspace_bytes - wt_bytes,
+                     (cudaStream_t)stream);
 }

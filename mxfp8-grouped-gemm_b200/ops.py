@@ -169,3 +169,64 @@ def transpose_u8(x: torch.Tensor) -> torch.Tensor:
     _lib.check(_lib.load().mxg_transpose_u8(x.data_ptr(), R, C, y.data_ptr(),
                                             _lib.stream_ptr(x.device)), "mxg_transpose_u8")
     return y
+
+
+# ---------------------------------------------------------------- two-phase plans
+class GroupedFwdPlan:
+    """Groups and packed scales of one grouped forward, prepared once in a
+    workspace owned by the plan; ``run`` launches only the tensor-core kernel."""
+
+    def __init__(self, a_scales, w_scales, offs, num_groups, M, N, K, device,
+                 offs_kind=_lib.OFFS_AUTO):
+        L = _lib.load()
+        self.E, self.M, self.N, self.K = int(num_groups), int(M), int(N), int(K)
+        self.a_scales = _scales(a_scales, "a_scales", (M, K // 32))
+        self.w_scales = _scales(w_scales, "w_scales", (num_groups, N, K // 32))
+        self.offs = _offs(offs, device)
+        self.ws = torch.empty(max(L.mxg_grouped_fwd_workspace_size(self.E, M, N, K), 1024),
+                              dtype=torch.uint8, device=device)
+        _lib.check(L.mxg_grouped_fwd_prepare(_lib.ptr(self.a_scales), _lib.ptr(self.w_scales),
+                                             self.offs.data_ptr(), self.offs.numel(), offs_kind,
+                                             self.E, M, N, K, self.ws.data_ptr(), self.ws.numel(),
+                                             _lib.stream_ptr(device)), "mxg_grouped_fwd_prepare")
+
+    def run(self, a, w, out=None, out_dtype=torch.bfloat16):
+        a = _operand(a, "a_fp8")
+        w = _operand(w, "w_fp8")
+        if out is None:
+            out = torch.empty(self.M, self.N, dtype=out_dtype, device=a.device)
+        _lib.check(_lib.load().mxg_grouped_fwd_run(
+            a.data_ptr(), w.data_ptr(), self.E, self.M, self.N, self.K, out.data_ptr(),
+            _out_code(out.dtype), self.ws.data_ptr(), self.ws.numel(), _lib.stream_ptr(a.device)),
+            "mxg_grouped_fwd_run")
+        return out
+
+
+class GroupedWgradPlan:
+    """Groups and packed scales of one grouped weight gradient (the
+    counterpart of the reference's wgrad_prepare, without operand copies)."""
+
+    def __init__(self, go_scales, ia_scales, offs, num_groups, M, N, K, device,
+                 offs_kind=_lib.OFFS_AUTO):
+        L = _lib.load()
+        self.E, self.M, self.N, self.K = int(num_groups), int(M), int(N), int(K)
+        self.go_scales = _scales(go_scales, "go_scales", (N, M // 32))
+        self.ia_scales = _scales(ia_scales, "ia_scales", (K, M // 32))
+        self.offs = _offs(offs, device)
+        self.ws = torch.empty(max(L.mxg_grouped_wgrad_workspace_size(self.E, M, N, K), 1024),
+                              dtype=torch.uint8, device=device)
+        _lib.check(L.mxg_grouped_wgrad_prepare(_lib.ptr(self.go_scales), _lib.ptr(self.ia_scales),
+                                               self.offs.data_ptr(), self.offs.numel(), offs_kind,
+                                               self.E, M, N, K, self.ws.data_ptr(), self.ws.numel(),
+                                               _lib.stream_ptr(device)), "mxg_grouped_wgrad_prepare")
+
+    def run(self, go, ia, out=None, out_dtype=torch.bfloat16):
+        go = _operand(go, "go")
+        ia = _operand(ia, "ia")
+        if out is None:
+            out = torch.empty(self.E, self.N, self.K, dtype=out_dtype, device=go.device)
+        _lib.check(_lib.load().mxg_grouped_wgrad_run(
+            go.data_ptr(), ia.data_ptr(), self.E, self.M, self.N, self.K, out.data_ptr(),
+            _out_code(out.dtype), self.ws.data_ptr(), self.ws.numel(), _lib.stream_ptr(go.device)),
+            "mxg_grouped_wgrad_run")
+        return out

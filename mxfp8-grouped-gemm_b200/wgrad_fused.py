@@ -8,8 +8,9 @@ result is ``grad_W[g] = GO[g] @ IA[g]^T`` of shape ``(E, N, K)``.
 The reference stacks per-expert copies of both operands before reusing its
 forward kernel (``wgrad_fused.py:48-62``) and assumes equal groups
 (``:46``).  Here the sm_100a kernel contracts each expert's token range in
-place, so ``wgrad_prepare`` makes no copies: it only validates and packages
-the inputs.  ``offs`` may be ``[E]`` group sizes (the reference docstring,
+place, so ``wgrad_prepare`` makes no copies: it schedules the groups and packs
+the scales once on the device, and ``wgrad_kernel`` launches only the
+tensor-core kernel.  ``offs`` may be ``[E]`` group sizes (the reference docstring,
 ``wgrad_fused.py:37``) or ``[E]`` cumulative ends (``e2e_bench.py:42``);
 boundaries must be multiples of 32 tokens.
 """
@@ -27,21 +28,28 @@ def wgrad_fused(go, ia, offs, go_scales=None, ia_scales=None, *, out_dtype=torch
 
 
 def wgrad_prepare(go, ia, offs, go_scales=None, ia_scales=None):
-    """Package the operands for ``wgrad_kernel`` (no copies)."""
+    """Prepare once: schedule the groups and pack the scales on the device
+    (no operand copies).  Returns the reference's dict plus the plan."""
     N, M = go.shape
     K = ia.shape[0]
     E = offs.shape[0]
-    offs_dev = offs.to(device=go.device, dtype=torch.int32).contiguous()
+    if (go_scales is None) != (ia_scales is None):
+        go_scales = ia_scales = None
+    plan = ops.GroupedWgradPlan(go_scales, ia_scales, offs, E, M, N, K, go.device)
     return {
         'A': go, 'B': ia,
-        'offs': offs_dev,
+        'offs': plan.offs,
         'As': go_scales, 'Bs': ia_scales,
         'E': E, 'N': N, 'K': K, 'M': M,
         'flops': 2 * M * N * K,
+        'plan': plan,
     }
 
 
 def wgrad_kernel(data: dict, *, out_dtype=torch.bfloat16, **kwargs):
-    """Run the wgrad on prepared data -> (E, N, K)."""
-    return ops.grouped_wgrad(data['A'], data['B'], data['offs'], data['As'], data['Bs'],
-                             out_dtype=out_dtype, num_groups=data['E'])
+    """Run the wgrad kernel on prepared data -> (E, N, K)."""
+    plan = data.get('plan')
+    if plan is None:
+        return ops.grouped_wgrad(data['A'], data['B'], data['offs'], data['As'], data['Bs'],
+                                 out_dtype=out_dtype, num_groups=data['E'])
+    return plan.run(data['A'], data['B'], out_dtype=out_dtype)

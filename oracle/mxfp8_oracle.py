@@ -301,3 +301,14 @@ def rel_frobenius(x, ref) -> float:
 def round_to_bf16(x: np.ndarray) -> np.ndarray:
     """float64 -> nearest bf16 value (as float64), via fp32."""
     return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
+
+
+def dequantize_torch(q, s):
+    """torch CPU fp32 dequantisation (the reference's own torch path,
+    ``scale_correctness.py:110-137`` / ``fused_fwd.py:249-264`` without the
+    bf16 rounding): codes uint8 [R, C] + scales uint8 [R, C/32] -> fp32."""
+    import torch
+    R, C = q.shape
+    v = q.contiguous().view(torch.float8_e4m3fn).to(torch.float32).view(R, C // BLOCK, BLOCK)
+    sc = torch.exp2(s.to(torch.float32) - float(E8M0_BIAS)).unsqueeze(-1)
+    return (v * sc).view(R, C)
