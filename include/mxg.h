@@ -114,6 +114,25 @@ MXG_API int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups, in
                                 int64_t k, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* Grouped forward for callers that cannot allocate device memory (a plugin
+ * inside a framework that owns the device memory pool, or host code that must
+ * not call cudaMalloc): same arguments and result as mxg_grouped_fwd, minus
+ * the workspace.  No counterpart in the reference.  Its scratch is a fixed
+ * array of MXG_NOALLOC_SCRATCH_BYTES inside this library, present on every GPU
+ * that loads the library until the process exits; problems whose
+ * mxg_grouped_fwd_workspace_size() exceeds it return
+ * MXG_ERR_WORKSPACE_TOO_SMALL.  The first call on a device looks up that
+ * array's device address (make it before any stream capture).  All calls on
+ * a device share the one array: calls that overlap on the GPU (different
+ * streams, or different host threads) race; run them in order on one stream.
+ * Nothing in the array needs to start zeroed: each call rewrites what it reads.
+ * It calls no cudaMalloc/cudaFree. */
+#define MXG_NOALLOC_SCRATCH_BYTES (64u << 20)
+MXG_API int mxg_grouped_fwd_noalloc(const void* a, const void* a_scales, const void* w,
+                                    const void* w_scales, const int32_t* offs, int offs_len,
+                                    int offs_kind, int num_groups, int64_t m, int64_t n, int64_t k,
+                                    void* out, int out_dtype, void* stream);
+
 /* ---- dense forward with a K x N weight: out[m, n] = x[m, k] . w[k, n] -------
  * Unit scales (the reference's fwd_ge passes none, fwd_final.py:101-106).
  * Replaces fwd_final.py:121-131 fwd_ge. */

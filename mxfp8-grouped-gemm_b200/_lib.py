@@ -43,6 +43,8 @@ _PROTOS = {
                                            _c_i64, _vp, _c_size, _vp]),
     "mxg_grouped_wgrad_run": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,
                                        _c_size, _vp]),
+    "mxg_grouped_fwd_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64,
+                                         _c_i64, _c_i64, _vp, _c_int, _vp]),
     "mxg_dense_fwd_kn_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "mxg_dense_fwd_kn": (_c_int, [_vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp, _c_size, _vp]),
     "mxg_grouped_wgrad_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64]),

@@ -975,3 +975,50 @@ extern "C" int mxg_dense_fwd_kn(const void* x, const void* w_kn, int64_t m, int6
   return run_grouped(P, wt, n, x, m, out, out_dtype, n, wt + wt_bytes, workspace_bytes - wt_bytes,
                      (cudaStream_t)stream);
 }
+
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers cannot allocate device memory themselves: plugins hosted by a
+// framework that owns the whole device memory pool, or host code that must
+// not call cudaMalloc (it may synchronise the device).  For them the grouped
+// forward can run on a scratch area built into this library: a fixed device
+// array in this file, one copy on every GPU that loads the library, held
+// until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(MXG_NOALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+static void* noalloc_scratch(int* status) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = MXG_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = MXG_ERR_CUDA;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+extern "C" int mxg_grouped_fwd_noalloc(const void* a, const void* a_scales, const void* w,
+                                       const void* w_scales, const int32_t* offs, int offs_len,
+                                       int offs_kind, int num_groups, int64_t m, int64_t n,
+                                       int64_t k, void* out, int out_dtype, void* stream) {
+  const size_t need = mxg_grouped_fwd_workspace_size(num_groups, m, n, k);
+  if (need > kNoAllocScratchBytes) return MXG_ERR_WORKSPACE_TOO_SMALL;
+  int st = MXG_OK;
+  void* scratch = noalloc_scratch(&st);
+  if (scratch == nullptr) return st;
+  return mxg_grouped_fwd(a, a_scales, w, w_scales, offs, offs_len, offs_kind, num_groups, m, n, k,
+                         out, out_dtype, scratch, kNoAllocScratchBytes, stream);
+}
