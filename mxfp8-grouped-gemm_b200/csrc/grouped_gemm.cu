@@ -1,4 +1,4 @@
-// Grouped MXFP8 GEMM for sm_100a (tcgen05 block-scaled MMA, TMA, TMEM).
+// Grouped MXFP8 GEMM for sm_100a (tcgen05 block-scaled MMA on CTA pairs, TMA, TMEM).
 //
 // One kernel serves both hot-path contractions.  Each computes, per group e,
 //     D[i, j] = sum_k A[i, k] * B[j, k]       (both operands K-contiguous)
@@ -11,15 +11,19 @@
 //       columns), k = the group's token range read in place from the
 //       token-contiguous operands; stored row-major into dW[e].
 //
-// Pipeline per persistent CTA (one per SM, 192 threads):
-//   warp 4  TMA producer: A tile 128 x 128 B, B tile up to 240 x 128 B
-//           (128-byte swizzle) and the two pre-packed scale chunks, into a
-//           4-stage shared-memory ring (mbarrier tx counts).
-//   warp 5  TMEM owner + single-thread MMA issuer: copies the stage's scale
-//           factors shared->TMEM (tcgen05.cp 32x128b.warpx4) and issues
-//           tcgen05.mma kind::mxf8f6f4.block_scale (M=128, N<=240, K=32).
-//   warps 0-3 epilogue: tcgen05.ld 32x32b, convert, store; the accumulator
-//           is double-buffered in TMEM so the epilogue of tile i overlaps
+// Each cluster of two CTAs (one per SM) works as a pair on 256 A rows x up to
+// 240 B rows: every CTA loads its own 128 A rows and half of the B rows, so an
+// SM moves a third fewer operand bytes per MMA than a lone CTA would, and the
+// leader CTA issues tcgen05.mma.cta_group::2 (M=256) whose accumulator rows
+// land in each CTA's own TMEM.  No load uses multicast.
+//   warp 4  TMA producer (both CTAs): A 128 x 128 B, B 120 x 128 B (128-byte
+//           swizzle) and the pre-packed scale chunks, into a 6-stage ring;
+//           completions are counted on the leader's barrier (.cta_group::2).
+//   warp 5  TMEM (512 columns, pair allocation); in the leader one thread
+//           copies the stage's scale factors to both TMEMs (tcgen05.cp) and
+//           issues the MMAs; commits release both CTAs' stages (multicast).
+//   warps 0-3 epilogue of each CTA: tcgen05.ld 32x32b, convert, store; the
+//           accumulator is double-buffered so the epilogue of tile i overlaps
 //           the main loop of tile i+1.
 // Every mbarrier wait is bounded (MXG_ERR_DEVICE_TIMEOUT, then unwind).
 #include <cuda.h>
@@ -36,20 +40,24 @@
 
 namespace mxg {
 
-constexpr int kBM = 128;                 // A rows per tile (MMA M)
-constexpr int kBNMax = 240;              // max B rows per tile (MMA N)
+constexpr int kBM = 128;                 // A rows per CTA (a pair covers 256)
+constexpr int kBNMax = 240;              // max B rows per pair tile (MMA N)
+constexpr int kBHalf = kBNMax / 2;       // B rows each CTA of the pair loads
 constexpr int kBK = 128;                 // contraction bytes per stage
-constexpr int kStages = 4;
+constexpr int kStages = 6;  // even: alternate stages use alternate scale buffers
 constexpr int kABytes = kBM * kBK;       // 16 KiB
-constexpr int kBBytes = kBNMax * kBK;    // 30 KiB
+constexpr int kBBytes = kBHalf * kBK;    // 15 KiB
 constexpr int kSfaBytes = 512;           // 128 rows x 4 scales, UTCCP layout
 constexpr int kSfbBytes = 1024;          // 2 x (128 rows x 4 scales)
-constexpr uint32_t kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+constexpr uint32_t kStageTxPerCta = kABytes + kBBytes + kSfaBytes + kSfbBytes;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;     // accumulator buffer i at column 256*i
-constexpr uint32_t kSfaCol = 240;        // 4 columns
-constexpr uint32_t kSfbCol = 244;        // 8 columns
+// Scale factors live in two TMEM buffers used by alternate stages, so the
+// copy for stage s+1 never overwrites columns the MMAs of stage s still read:
+// buffer 0 in columns 240-251, buffer 1 in 496-507 (SFA 4 columns, SFB 8).
+constexpr uint32_t kSfCol0 = 240, kSfCol1 = 496;
+constexpr uint32_t kSfbOff = 4;
 
 enum { MODE_FWD = 0, MODE_WGRAD = 1 };
 
@@ -181,7 +189,7 @@ __global__ void __launch_bounds__(MXG_MAX_GROUPS) schedule_kernel(SchedArgs a) {
   const bool any_bad = __syncthreads_or(bad);
   // per-group work counts
   int nt = 0, kb = 0, tiles = 0, asf = 0, bsf = 0;
-  const int mb = ceil_div(a.n_out, kBM);
+  const int mbp = ceil_div(a.n_out, 2 * kBM);  // pairs of 128-row A blocks
   if (tid < E && !any_bad) {
     if (a.mode == MODE_FWD) {
       nt = ceil_div(len, kBNMax);
@@ -190,8 +198,8 @@ __global__ void __launch_bounds__(MXG_MAX_GROUPS) schedule_kernel(SchedArgs a) {
       nt = ceil_div(a.n_ext, kBNMax);
       kb = ceil_div(len, kBK);
     }
-    tiles = mb * nt;
-    asf = mb * kb;
+    tiles = mbp * nt;
+    asf = 2 * mbp * kb;  // every pair has two A blocks (the second may be past n_out)
     bsf = nt * kb;
   }
   int t_tot, a_tot, b_tot;
@@ -305,21 +313,10 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
   }
 }
 
-// Forward: rows [meta[3], M) belong to no group -> write zeros.
-__global__ void zero_tail_kernel(const int* meta, uint8_t* out, int64_t M, int64_t row_bytes) {
-  const int64_t first = meta[3];
-  if (first >= M) return;
-  const int64_t beg = first * row_bytes, end = M * row_bytes;
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  for (int64_t i = beg + (int64_t(blockIdx.x) * blockDim.x + threadIdx.x); i < end; i += stride)
-    out[i] = 0;
-}
 
-// ---------------------------------------------------------------- GEMM kernel
+// ---------------------------------------------------------------- GEMM kernel (CTA pairs)
 struct GemmArgs {
   const int* meta;
-  const uint8_t* sfa_pack;
-  const uint8_t* sfb_pack;
   void* out;
   int out_dtype;
   int E;
@@ -337,10 +334,10 @@ struct __align__(1024) SmemLayout {
   uint8_t b[kStages][kBBytes];
   uint8_t sfa[kStages][kSfaBytes];
   uint8_t sfb[kStages][kSfbBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
+  uint64_t full[kStages];      // leader: both CTAs' loads of the stage landed
+  uint64_t empty[kStages];     // each CTA: the pair MMA finished reading the stage
+  uint64_t acc_full[2];        // each CTA: accumulator buffer complete
+  uint64_t acc_empty[2];       // leader: both CTAs' epilogues drained the buffer
   uint64_t drain;
   uint64_t never;
   uint32_t tmem_base;
@@ -355,13 +352,17 @@ struct __align__(1024) SmemLayout {
   int g_bsf[MXG_MAX_GROUPS + 1];
 };
 constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct TileInfo {
   int e, mb, nt, n0, nlen, kb_count, klen, k0, a_row, b_row, sfa0, sfb0;
 };
 
+// Pair tile t as seen by CTA `rank` of the pair: its own 128-row A block
+// (mb = 2 * pair block + rank) and the pair's B rows [b_row, b_row + nlen).
 template <int MODE>
-__device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmArgs& g, int t) {
+__device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmArgs& g, int t,
+                                                int rank) {
   TileInfo ti;
   int lo = 0, hi = g.E - 1;
   while (lo < hi) {
@@ -371,8 +372,9 @@ __device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmA
   ti.e = lo;
   const int local = t - s.tile_start[lo];
   const int nt_count = s.g_nt[lo];
-  ti.mb = local / nt_count;
-  ti.nt = local - ti.mb * nt_count;
+  const int mbp = local / nt_count;
+  ti.nt = local - mbp * nt_count;
+  ti.mb = 2 * mbp + rank;
   const int ext = MODE == MODE_FWD ? s.g_len[lo] : g.n_ext;
   split_rows(ext, nt_count, ti.nt, ti.n0, ti.nlen);
   ti.kb_count = s.g_kb[lo];
@@ -392,13 +394,34 @@ __device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmA
   return ti;
 }
 
+// decode_tile for a whole warp, every field broadcast from lane 0 so the
+// compiler can keep tile coordinates in uniform registers.
+template <int MODE>
+__device__ __forceinline__ TileInfo decode_tile_warp(const SmemLayout& s, const GemmArgs& g, int t,
+                                                     int rank) {
+  TileInfo ti = decode_tile<MODE>(s, g, t, rank);
+  ti.e = __shfl_sync(0xffffffffu, ti.e, 0);
+  ti.mb = __shfl_sync(0xffffffffu, ti.mb, 0);
+  ti.nt = __shfl_sync(0xffffffffu, ti.nt, 0);
+  ti.n0 = __shfl_sync(0xffffffffu, ti.n0, 0);
+  ti.nlen = __shfl_sync(0xffffffffu, ti.nlen, 0);
+  ti.kb_count = __shfl_sync(0xffffffffu, ti.kb_count, 0);
+  ti.klen = __shfl_sync(0xffffffffu, ti.klen, 0);
+  ti.k0 = __shfl_sync(0xffffffffu, ti.k0, 0);
+  ti.a_row = __shfl_sync(0xffffffffu, ti.a_row, 0);
+  ti.b_row = __shfl_sync(0xffffffffu, ti.b_row, 0);
+  ti.sfa0 = __shfl_sync(0xffffffffu, ti.sfa0, 0);
+  ti.sfb0 = __shfl_sync(0xffffffffu, ti.sfb0, 0);
+  return ti;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
 // Epilogue store of 32 accumulator columns [c0, c0+32) held by this thread
-// (TMEM lane = `row` of the tile).
+// (TMEM lane = `row` of this CTA's 128-row block).
 template <int MODE>
 __device__ __forceinline__ void store_chunk(const GemmArgs& g, const TileInfo& ti, int row, int c0,
                                             const uint32_t (&v)[32], bool zero) {
@@ -465,11 +488,16 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& g, const TileInfo& t
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmSFA,
+                        const __grid_constant__ CUtensorMap tmSFB, GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   SmemLayout& s = *reinterpret_cast<SmemLayout*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = int(cluster_ctarank());
+  const int pair = int(cluster_id_x());
+  const int npairs = int(num_clusters_x());
 
   MetaView mv{const_cast<int*>(g.meta), g.E};
   for (int i = threadIdx.x; i <= g.E; i += kThreads) {
@@ -494,97 +522,110 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&s.acc_full[i]), 1);
-      mbar_init(smem_u32(&s.acc_empty[i]), 4 * 32);
+      mbar_init(smem_u32(&s.acc_empty[i]), 2 * 4);  // one arrival per epilogue warp, both CTAs
     }
     mbar_init(smem_u32(&s.drain), 1);
     mbar_init(smem_u32(&s.never), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmSFA);
+    tma_prefetch_desc(&tmSFB);
   }
   if (warp == 5) {
-    tmem_alloc(smem_u32(&s.tmem_base), kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(&s.tmem_base), kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
   const int num_tiles = s.num_tiles;
-  WaitCtl wc{&s.abort_flag, g.err, g.timeout_ns};
+  WaitCtl wc{&s.abort_flag, g.err, g.timeout_ns, mapa_shared(smem_u32(&s.abort_flag), rank ^ 1)};
 
   if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      uint32_t stage = 0, phase = 0, armed = 0, armed_par = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile<MODE>(s, g, t);
-        for (int kb = 0; kb < ti.kb_count; ++kb) {
-          if (!mbar_wait(smem_u32(&s.empty[stage]), phase ^ 1u, wc)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_u32(&s.full[stage]);
-          mbar_arrive_expect_tx(fb, kStageTx);
+    // ------------------------------------------------------------ producer (both CTAs)
+    // The whole warp runs the loop (tile fields stay warp-uniform); one
+    // elected lane issues the copies.
+    uint32_t stage = 0, phase = 0, armed = 0, armed_par = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += npairs) {
+      const TileInfo ti = decode_tile_warp<MODE>(s, g, t, rank);
+      const int half = int((uint32_t(ti.nlen + 15) & ~15u) >> 1);
+      for (int kb = 0; kb < ti.kb_count; ++kb) {
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.empty[stage]), phase ^ 1u, wc))) {
+          ok = false;
+          break;
+        }
+        if (elect_one_sync()) {
+          const uint32_t fb_local = smem_u32(&s.full[stage]);
+          if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kStageTxPerCta);
+          const uint32_t fb = mapa_shared(fb_local, 0);
           const int x = ti.k0 + kb * kBK;
-          tma_load_2d(smem_u32(s.a[stage]), &tmA, x, ti.a_row, fb);
-          tma_load_2d(smem_u32(s.b[stage]), &tmB, x, ti.b_row, fb);
-          bulk_load(smem_u32(s.sfa[stage]), g.sfa_pack + int64_t(ti.sfa0 + kb) * kSfaBytes,
-                    kSfaBytes, fb);
-          bulk_load(smem_u32(s.sfb[stage]), g.sfb_pack + int64_t(ti.sfb0 + kb) * kSfbBytes,
-                    kSfbBytes, fb);
-          armed |= 1u << stage;
-          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          tma_load_2d_pair(smem_u32(s.a[stage]), &tmA, x, ti.a_row, fb);
+          tma_load_2d_pair(smem_u32(s.b[stage]), &tmB, x, ti.b_row + rank * half, fb);
+          tma_load_2d_pair(smem_u32(s.sfa[stage]), &tmSFA, 0, ti.sfa0 + kb, fb);
+          tma_load_2d_pair(smem_u32(s.sfb[stage]), &tmSFB, 0, 2 * (ti.sfb0 + kb), fb);
+        }
+        __syncwarp();
+        armed |= 1u << stage;
+        armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      if (!ok) {  // unwinding: let the copies already issued land first
-        for (int i = 0; i < kStages; ++i)
-          if (armed & (1u << i)) mbar_drain(smem_u32(&s.full[i]), (armed_par >> i) & 1u, 20000000ull);
-      }
+    }
+    if (!ok && rank == 0 && lane == 0) {  // unwinding: let the copies already counted here land
+      for (int i = 0; i < kStages; ++i)
+        if (armed & (1u << i)) mbar_drain(smem_u32(&s.full[i]), (armed_par >> i) & 1u, 20000000ull);
     }
   } else if (warp == 5) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    // The whole warp runs the loop so descriptors and TMEM addresses are
+    // warp-uniform; one elected lane issues the tcgen05 instructions (issuing
+    // from a lone active lane costs about as much per MMA as the MMA itself).
+    if (rank == 0) {
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true, issued = false;
-      if (g.stall_test) ok = mbar_wait(smem_u32(&s.never), 0, wc);
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile<MODE>(s, g, t);
+      if (g.stall_test) ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.never), 0, wc));
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        const TileInfo ti = decode_tile_warp<MODE>(s, g, t, 0);
         if (ti.kb_count == 0) continue;
-        if (!mbar_wait(smem_u32(&s.acc_empty[acc]), acc_phase ^ 1u, wc)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.acc_empty[acc]), acc_phase ^ 1u, wc))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccStride;
         const uint32_t n_mma = uint32_t(ti.nlen + 15) & ~15u;
-        const uint32_t idesc0 = make_idesc_mxf8(kBM, n_mma);
-        const uint32_t sfa_t = tmem_base + kSfaCol, sfb_t = tmem_base + kSfbCol;
+        const uint32_t idesc0 = make_idesc_mxf8(2 * kBM, n_mma);
         for (int kb = 0; kb < ti.kb_count; ++kb) {
-          if (!mbar_wait(smem_u32(&s.full[stage]), phase, wc)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.full[stage]), phase, wc))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t sfa_t = tmem_base + ((stage & 1u) ? kSfCol1 : kSfCol0);
+          const uint32_t sfb_t = sfa_t + kSfbOff;
           const uint32_t sfa_s = smem_u32(s.sfa[stage]), sfb_s = smem_u32(s.sfb[stage]);
-          tc_cp_32x128b_warpx4(sfa_t, sdesc_sf_chunk(sfa_s));
-          tc_cp_32x128b_warpx4(sfb_t, sdesc_sf_chunk(sfb_s));
-          tc_cp_32x128b_warpx4(sfb_t + 4, sdesc_sf_chunk(sfb_s + 512));
           const int rem = ti.klen - kb * kBK;
           const int nk = rem >= kBK ? 4 : rem / 32;
           const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(s.a[stage]));
           const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(s.b[stage]));
-          for (int kk = 0; kk < nk; ++kk) {
-            tc_mma_mxf8(d_tmem, adesc + uint64_t(2 * kk), bdesc + uint64_t(2 * kk),
-                        idesc_with_sf_id(idesc0, kk, kk), sfa_t | (uint32_t(kk) << 30),
-                        sfb_t | (uint32_t(kk) << 30), (kb | kk) != 0 ? 1u : 0u);
+          if (elect_one_sync()) {
+            tc_cp_32x128b_warpx4_pair(sfa_t, sdesc_sf_chunk(sfa_s));
+            tc_cp_32x128b_warpx4_pair(sfb_t, sdesc_sf_chunk(sfb_s));
+            tc_cp_32x128b_warpx4_pair(sfb_t + 4, sdesc_sf_chunk(sfb_s + 512));
+            for (int kk = 0; kk < nk; ++kk) {
+              tc_mma_mxf8_pair(d_tmem, adesc + uint64_t(2 * kk), bdesc + uint64_t(2 * kk),
+                               idesc_with_sf_id(idesc0, kk, kk), sfa_t | (uint32_t(kk) << 30),
+                               sfb_t | (uint32_t(kk) << 30), (kb | kk) != 0 ? 1u : 0u);
+            }
+            tc_commit_pair_mc(smem_u32(&s.empty[stage]), 0x3);
           }
-          tc_commit(smem_u32(&s.empty[stage]));
+          __syncwarp();
           issued = true;
           if (++stage == kStages) {
             stage = 0;
@@ -592,21 +633,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        tc_commit(smem_u32(&s.acc_full[acc]));
+        if (elect_one_sync()) tc_commit_pair_mc(smem_u32(&s.acc_full[acc]), 0x3);
+        __syncwarp();
         acc ^= 1u;
         if (acc == 0) acc_phase ^= 1u;
       }
       if (issued) {  // every MMA done before TMEM is released
-        tc_commit(smem_u32(&s.drain));
+        if (elect_one_sync()) tc_commit_pair(smem_u32(&s.drain));
+        __syncwarp();
         mbar_drain(smem_u32(&s.drain), 0, 50000000ull);
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 0-3)
+    // ------------------------------------------------------------ epilogue (warps 0-3, both CTAs)
     const int row = warp * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile<MODE>(s, g, t);
+    for (int t = pair; t < num_tiles; t += npairs) {
+      const TileInfo ti = decode_tile<MODE>(s, g, t, rank);
       uint32_t v[32];
       if (ti.kb_count == 0) {  // empty group (wgrad): dW[e] = 0
         for (int c0 = 0; c0 < ti.nlen; c0 += 32) store_chunk<MODE>(g, ti, row, c0, v, true);
@@ -623,18 +666,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         store_chunk<MODE>(g, ti, row, c0, v, false);
       }
       tc_fence_before();
-      mbar_arrive(smem_u32(&s.acc_empty[acc]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[acc]), 0));
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
   }
 
+  if (s.abort_flag) {  // unwinding: give copies issued by either CTA time to land
+    const uint64_t until = globaltimer_ns() + 2000000ull;
+    while (globaltimer_ns() < until) {
+    }
+  }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // the peer no longer touches this CTA's barriers or TMEM
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  cluster_sync_all();
+}
+
+// Forward: rows [meta[3], M) belong to no group -> write zeros.
+__global__ void zero_tail_kernel(const int* meta, uint8_t* out, int64_t M, int64_t row_bytes) {
+  const int64_t first = meta[3];
+  if (first >= M) return;
+  const int64_t beg = first * row_bytes, end = M * row_bytes;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = beg + (int64_t(blockIdx.x) * blockDim.x + threadIdx.x); i < end; i += stride)
+    out[i] = 0;
 }
 
 // ---------------------------------------------------------------- host side
@@ -652,7 +713,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D uint8 tensor [rows, cols] (cols contiguous), box {128 bytes, box_rows},
+// 2-D uint8 operand [rows, cols] (cols contiguous), box {128 bytes, box_rows},
 // 128-byte swizzle; out-of-range elements read as zero.
 static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t cols, int box_rows) {
   auto enc = get_encode_fn();
@@ -667,26 +728,44 @@ static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t co
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
+// Packed scale chunks viewed as rows of 128 uint32 (512 bytes), box of
+// `box_rows` rows, no swizzle.
+static int make_sf_tmap(CUtensorMap* tm, const void* base, int64_t rows, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return MXG_ERR_CUDA;
+  cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+  cuuint64_t strides[1] = {512};
+  cuuint32_t box[2] = {128, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
+}
+
 struct WsLayout {
   size_t meta_off, sfa_off, sfb_off, total;
+  int64_t sfa_chunks, sfb_chunks;
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 static WsLayout ws_layout(int mode, int E, int64_t M, int64_t n_out, int64_t n_ext, int64_t K) {
-  const int64_t mb = (n_out + kBM - 1) / kBM;
+  const int64_t mb2 = 2 * ((n_out + 2 * kBM - 1) / (2 * kBM));  // A blocks, rounded to pairs
   int64_t asf, bsf;
   if (mode == MODE_FWD) {
     const int64_t kb = (K + kBK - 1) / kBK;
-    asf = int64_t(E) * mb * kb;
+    asf = int64_t(E) * mb2 * kb;
     bsf = kb * ((M + int64_t(kBNMax - 1) * E) / kBNMax + 1);
   } else {
     const int64_t kbs = (M + int64_t(kBK - 1) * E) / kBK + 1;
     const int64_t nt = (n_ext + kBNMax - 1) / kBNMax;
-    asf = mb * kbs;
+    asf = mb2 * kbs;
     bsf = nt * kbs;
   }
   WsLayout w;
+  w.sfa_chunks = asf;
+  w.sfb_chunks = bsf;
   w.meta_off = 0;
   w.sfa_off = align_up(MetaView::words(E) * 4, 1024);
   w.sfb_off = align_up(w.sfa_off + size_t(asf) * kSfaBytes, 1024);
@@ -694,18 +773,36 @@ static WsLayout ws_layout(int mode, int E, int64_t M, int64_t n_out, int64_t n_e
   return w;
 }
 
-static int configure_kernels() {
-  static bool done[64] = {false};
+// Per device: kernel attributes and the number of CTA pairs that fit at once.
+static int configure_kernels(int* pairs) {
+  static std::mutex mu;
+  static int cached_pairs[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return MXG_ERR_CUDA;
-  if (dev < 64 && done[dev]) return MXG_OK;
-  if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_FWD>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
-    return MXG_ERR_CUDA;
-  if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_WGRAD>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
-    return MXG_ERR_CUDA;
-  if (dev < 64) done[dev] = true;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MXG_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cached_pairs[dev] == 0) {
+    if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_FWD>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(grouped_gemm_kernel<MODE_WGRAD>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
+      return MXG_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_kernel<MODE_FWD>, &cfg) != cudaSuccess || n < 1)
+      return MXG_ERR_CUDA;
+    cached_pairs[dev] = n;
+  }
+  *pairs = cached_pairs[dev];
   return MXG_OK;
 }
 
@@ -757,21 +854,24 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   if (ws_bytes < L.total) return MXG_ERR_WORKSPACE_TOO_SMALL;
   int st = check_device();
   if (st) return st;
-  st = configure_kernels();
+  int pairs = 0;
+  st = configure_kernels(&pairs);
   if (st) return st;
   uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
   int* meta = reinterpret_cast<int*>(wsb + L.meta_off);
   int* err = device_error_word();
   if (!err) return MXG_ERR_CUDA;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmSFA, tmSFB;
   st = make_tmap(&tmA, a_ptr, a_rows, P.kc, kBM);
   if (st) return st;
-  st = make_tmap(&tmB, b_ptr, b_rows, P.kc, kBNMax);
+  st = make_tmap(&tmB, b_ptr, b_rows, P.kc, kBHalf);
+  if (st) return st;
+  st = make_sf_tmap(&tmSFA, wsb + L.sfa_off, std::max<int64_t>(L.sfa_chunks, 1), 1);
+  if (st) return st;
+  st = make_sf_tmap(&tmSFB, wsb + L.sfb_off, std::max<int64_t>(2 * L.sfb_chunks, 2), 2);
   if (st) return st;
   GemmArgs ga;
   ga.meta = meta;
-  ga.sfa_pack = wsb + L.sfa_off;
-  ga.sfb_pack = wsb + L.sfb_off;
   ga.out = out;
   ga.out_dtype = out_dtype;
   ga.E = P.E;
@@ -783,16 +883,32 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   const int64_t stall = take_injected_stall();
   ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
   ga.stall_test = stall > 0 ? 1 : 0;
-  const int sms = num_sms();
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(unsigned(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (P.mode == MODE_FWD) {
-    grouped_gemm_kernel<MODE_FWD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
-    const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
-    zero_tail_kernel<<<sms, 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
-                                               row_bytes);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, ga);
+    if (e == cudaSuccess) {
+      const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
+      zero_tail_kernel<<<num_sms(), 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
+                                                      row_bytes);
+      e = cudaGetLastError();
+    }
   } else {
-    grouped_gemm_kernel<MODE_WGRAD><<<sms, kThreads, kSmemBytes, stream>>>(tmA, tmB, ga);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_WGRAD>, tmA, tmB, tmSFA, tmSFB, ga);
   }
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 }  // namespace mxg
