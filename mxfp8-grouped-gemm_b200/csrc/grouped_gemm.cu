@@ -327,6 +327,7 @@ struct GemmArgs {
   int* err;
   uint64_t timeout_ns;
   int stall_test;
+  int fwd_tma_store;  // forward output row stride is 16-byte aligned: store via TMA
 };
 
 struct __align__(1024) SmemLayout {
@@ -334,6 +335,7 @@ struct __align__(1024) SmemLayout {
   uint8_t b[kStages][kBBytes];
   uint8_t sfa[kStages][kSfaBytes];
   uint8_t sfb[kStages][kSfbBytes];
+  uint8_t epi[4][4096];        // per epilogue warp: 32 rows x 128 B staging, 128-byte swizzle
   uint64_t full[kStages];      // leader: both CTAs' loads of the stage landed
   uint64_t empty[kStages];     // each CTA: the pair MMA finished reading the stage
   uint64_t acc_full[2];        // each CTA: accumulator buffer complete
@@ -490,7 +492,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmSFA,
-                        const __grid_constant__ CUtensorMap tmSFB, GemmArgs g) {
+                        const __grid_constant__ CUtensorMap tmSFB,
+                        const __grid_constant__ CUtensorMap tmOut,
+                        const __grid_constant__ CUtensorMap tmOut16, GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   SmemLayout& s = *reinterpret_cast<SmemLayout*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -648,6 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue (warps 0-3, both CTAs)
     const int row = warp * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
+    bool epi_pending = false;  // a TMA store of this warp may still read its staging buffer
     for (int t = pair; t < num_tiles; t += npairs) {
       const TileInfo ti = decode_tile<MODE>(s, g, t, rank);
       uint32_t v[32];
@@ -660,17 +665,74 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (uint32_t(warp * 32) << 16) + acc * kAccStride;
+      const bool tma_out = MODE == MODE_WGRAD && g.out_dtype == MXG_DTYPE_F32;
+      const bool f32 = g.out_dtype == MXG_DTYPE_F32;
       for (int c0 = 0; c0 < ti.nlen; c0 += 32) {
         tmem_ld_32x32b_x32(tb + uint32_t(c0), v);
         tmem_ld_wait();
-        store_chunk<MODE>(g, ti, row, c0, v, false);
+        if (c0 + 32 >= ti.nlen) {  // accumulator fully read: let the next tile's MMAs start
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[acc]), 0));
+        }
+        const int rows_here = min(32, ti.nlen - c0);
+        if (MODE == MODE_FWD && g.fwd_tma_store && (rows_here == 32 || rows_here == 16)) {
+          // forward: this warp holds 32 features (lanes) x 32 tokens (columns);
+          // stage it transposed as [token][feature] and store whole token rows
+          uint8_t* buf = s.epi[warp];
+          if (epi_pending) {
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+          if (f32) {  // 128-byte rows, 128-byte swizzle
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              *reinterpret_cast<uint32_t*>(buf + j * 128 + (((lane >> 2) ^ (j & 7)) * 16) +
+                                           (lane & 3) * 4) = v[j];
+          } else {    // 64-byte rows, 64-byte swizzle
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              *reinterpret_cast<__nv_bfloat16*>(buf + j * 64 + (((lane >> 3) ^ ((j >> 1) & 3)) * 16) +
+                                                (lane & 7) * 2) =
+                  __float2bfloat16_rn(__uint_as_float(v[j]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int f0 = ti.mb * kBM + warp * 32;
+            if (rows_here == 32) tma_store_2d(&tmOut, smem_u32(buf), f0, ti.b_row + c0);
+            else tma_store_2d(&tmOut16, smem_u32(buf), f0, ti.b_row + c0);
+            bulk_commit_group();
+          }
+          epi_pending = true;
+        } else if (tma_out && c0 + 32 <= ti.nlen) {
+          // stage this warp's 32 x 32 fp32 block (row = lane) in the 128-byte
+          // swizzled layout the store's tensor map expects, then one TMA store
+          uint8_t* buf = s.epi[warp];
+          if (epi_pending) {
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) * 16)) =
+                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmOut, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e);
+            bulk_commit_group();
+          }
+          epi_pending = true;
+        } else {
+          store_chunk<MODE>(g, ti, row, c0, v, false);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[acc]), 0));
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (epi_pending && lane == 0) bulk_wait_group0();
+    __syncwarp();
   }
 
   if (s.abort_flag) {  // unwinding: give copies issued by either CTA time to land
@@ -730,6 +792,39 @@ static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t co
 
 // Packed scale chunks viewed as rows of 128 uint32 (512 bytes), box of
 // `box_rows` rows, no swizzle.
+// Forward output y [M, N] (bf16 or fp32), box {32 features, box_rows tokens};
+// swizzle matches the staging layout (64-byte rows for bf16, 128 for fp32).
+static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, int out_dtype,
+                             int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return MXG_ERR_CUDA;
+  const bool f32 = out_dtype == MXG_DTYPE_F32;
+  const cuuint64_t esz = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(M)};
+  cuuint64_t strides[1] = {cuuint64_t(N) * esz};
+  cuuint32_t box[2] = {32, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
+}
+
+// dW [E, rows, cols] fp32 output, box {32 cols, 32 rows, 1}, 128-byte swizzle.
+static int make_out_tmap_f32(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols) {
+  auto enc = get_encode_fn();
+  if (!enc) return MXG_ERR_CUDA;
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(E)};
+  cuuint64_t strides[2] = {cuuint64_t(cols) * 4, cuuint64_t(cols) * 4 * cuuint64_t(rows)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
+}
+
 static int make_sf_tmap(CUtensorMap* tm, const void* base, int64_t rows, int box_rows) {
   auto enc = get_encode_fn();
   if (!enc) return MXG_ERR_CUDA;
@@ -870,6 +965,19 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   if (st) return st;
   st = make_sf_tmap(&tmSFB, wsb + L.sfb_off, std::max<int64_t>(2 * L.sfb_chunks, 2), 2);
   if (st) return st;
+  CUtensorMap tmOut = tmA, tmOut16 = tmA;  // epilogue store maps (unused ones stay dummies)
+  if (P.mode == MODE_WGRAD && out_dtype == MXG_DTYPE_F32) {
+    st = make_out_tmap_f32(&tmOut, out, P.E, P.n_out, P.n_ext);
+    if (st) return st;
+  }
+  // TMA stores need the output row stride (N elements) to be a multiple of 16 bytes
+  const bool fwd_tma = P.mode == MODE_FWD && (P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2)) % 16 == 0;
+  if (fwd_tma) {
+    st = make_out_tmap_fwd(&tmOut, out, P.M, P.n_out, out_dtype, 32);
+    if (st) return st;
+    st = make_out_tmap_fwd(&tmOut16, out, P.M, P.n_out, out_dtype, 16);
+    if (st) return st;
+  }
   GemmArgs ga;
   ga.meta = meta;
   ga.out = out;
@@ -883,6 +991,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   const int64_t stall = take_injected_stall();
   ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
   ga.stall_test = stall > 0 ? 1 : 0;
+  ga.fwd_tma_store = fwd_tma ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -898,7 +1007,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   cfg.numAttrs = 1;
   cudaError_t e;
   if (P.mode == MODE_FWD) {
-    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, ga);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, ga);
     if (e == cudaSuccess) {
       const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
       zero_tail_kernel<<<num_sms(), 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
@@ -906,7 +1015,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
       e = cudaGetLastError();
     }
   } else {
-    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_WGRAD>, tmA, tmB, tmSFA, tmSFB, ga);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_WGRAD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, ga);
   }
   return cuda_status(e);
 }

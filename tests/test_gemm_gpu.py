@@ -121,6 +121,7 @@ def test_offs_conventions_agree(mxg, orc, cuda_dev):
     ([1000], 384, 96),                       # one group, several token tiles, K < 128
     ([0, 0, 700], 128, 1024),                # leading empty groups
     ([33] * 9, 320, 288),                    # many small groups
+    ([100, 60], 132, 64),                    # N*2 bytes not a multiple of 16: direct-store epilogue
 ])
 def test_fwd_ragged(mxg, orc, cuda_dev, sizes, N, K):
     gen = torch.Generator(device=cuda_dev).manual_seed(sum(sizes) + N + K)
