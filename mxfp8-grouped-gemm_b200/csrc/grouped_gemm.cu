@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 
 #include "mxg.h"
@@ -44,7 +45,7 @@ constexpr int kBM = 128;                 // A rows per CTA (a pair covers 256)
 constexpr int kBNMax = 240;              // max B rows per pair tile (MMA N)
 constexpr int kBHalf = kBNMax / 2;       // B rows each CTA of the pair loads
 constexpr int kBK = 128;                 // contraction bytes per stage
-constexpr int kStages = 6;  // even: alternate stages use alternate scale buffers
+constexpr int kStages = 6;
 constexpr int kABytes = kBM * kBK;       // 16 KiB
 constexpr int kBBytes = kBHalf * kBK;    // 15 KiB
 constexpr int kSfaBytes = 512;           // 128 rows x 4 scales, UTCCP layout
@@ -335,7 +336,7 @@ struct __align__(1024) SmemLayout {
   uint8_t b[kStages][kBBytes];
   uint8_t sfa[kStages][kSfaBytes];
   uint8_t sfb[kStages][kSfbBytes];
-  uint8_t epi[4][4096];        // per epilogue warp: 32 rows x 128 B staging, 128-byte swizzle
+  alignas(1024) uint8_t epi[4][4096];  // per epilogue warp: 32 rows x 128 B staging, 128-byte swizzle
   uint64_t full[kStages];      // leader: both CTAs' loads of the stage landed
   uint64_t empty[kStages];     // each CTA: the pair MMA finished reading the stage
   uint64_t acc_full[2];        // each CTA: accumulator buffer complete
@@ -354,6 +355,11 @@ struct __align__(1024) SmemLayout {
   int g_bsf[MXG_MAX_GROUPS + 1];
 };
 constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;
+// swizzled tiles must start on 1024-byte boundaries (the swizzle pattern is
+// taken from address bits 4-9)
+static_assert(offsetof(SmemLayout, a) % 1024 == 0 && kABytes % 1024 == 0, "A tile alignment");
+static_assert(offsetof(SmemLayout, b) % 1024 == 0 && kBBytes % 1024 == 0, "B tile alignment");
+static_assert(offsetof(SmemLayout, epi) % 1024 == 0, "epilogue staging alignment");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct TileInfo {
@@ -591,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warp-uniform; one elected lane issues the tcgen05 instructions (issuing
     // from a lone active lane costs about as much per MMA as the MMA itself).
     if (rank == 0) {
-      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0, sf_buf = 0;
       bool ok = true, issued = false;
       if (g.stall_test) ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.never), 0, wc));
       for (int t = pair; t < num_tiles && ok; t += npairs) {
@@ -611,7 +617,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sfa_t = tmem_base + ((stage & 1u) ? kSfCol1 : kSfCol0);
+          const uint32_t sfa_t = tmem_base + (sf_buf ? kSfCol1 : kSfCol0);
+          sf_buf ^= 1u;
           const uint32_t sfb_t = sfa_t + kSfbOff;
           const uint32_t sfa_s = smem_u32(s.sfa[stage]), sfb_s = smem_u32(s.sfb[stage]);
           const int rem = ti.klen - kb * kBK;
@@ -680,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // forward: this warp holds 32 features (lanes) x 32 tokens (columns);
           // stage it transposed as [token][feature] and store whole token rows
           uint8_t* buf = s.epi[warp];
-          if (epi_pending) {
+          if (epi_pending) {  // the previous store has finished reading the buffer
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
           }
