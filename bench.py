@@ -13,8 +13,16 @@ the reference-facing API (group scheduler + scale packing + tensor-core
 kernel).  ``value`` = algorithmic FLOPs (2 * real rows * N * K) / time.
 All operands together exceed the 126 MB L2, so no explicit flush is needed.
 
-N>1 (torchrun, one rank per GPU): every rank runs the same per-GPU workload
-(weak scaling); the step time is the max over ranks.
+N>1 (torchrun, one rank per GPU): BASELINE config 5, the DeepSeek-V3 MoE
+expert layer under expert parallelism.  256 experts are sharded evenly (256/N
+per GPU, placed by expected load), each GPU routes 16384 tokens top-8 with
+Zipf(1.1) expert popularity, and one step is NCCL all-to-all dispatch ->
+MXFP8 quantise -> gate/up fwd -> swiglu -> down fwd -> combine, plus the
+backward weight gradients of both projections (dy dispatched along the same
+plan, down dgrad, swiglu backward).  Per-GPU work is fixed (weak scaling);
+``value`` = GEMM FLOPs of all ranks / the max-over-ranks step time.  The N=1
+line carries the same layer on one GPU (all 256 experts) as ``ep_layer_1gpu``
+for a like-for-like comparison.
 
 ``--impl reference`` times the reference's CPU path (torch dequantise + fp32
 matmul, restated in oracle/) on a bounded sample of the same workload.
@@ -143,8 +151,7 @@ class Workload:
     def __init__(self, seed=0, device="cuda", experts=None, rows=None):
         m = pkg()
         W = m.workloads
-        global E
-        E = experts or E
+        self.E = E = experts or globals()["E"]
         self.split = W.dirichlet_split(rows or ROUTED_ROWS, E, 1.0, seed=seed)
         sp = self.split
         self.M = sp.M
@@ -177,8 +184,8 @@ class Workload:
     def gemm_calls(self):
         """The three API calls of one step, each as (name, prepare, run)."""
         m = pkg()
-        ops = m.ops
         L = m._lib.load()
+        E = self.E
         s = lambda: m._lib.stream_ptr()
         ws_f = m._lib.workspace(L.mxg_grouped_fwd_workspace_size(E, self.M, GATE_UP, HIDDEN), self.y.device)
         self._ws = {"f": ws_f}
@@ -365,6 +372,181 @@ def sample_experts(wl, n=2):
     return sorted(int(i) for i in order[mid - n // 2: mid - n // 2 + n])
 
 
+
+# ---------------------------------------------------------------- EP layer (config 5)
+EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
+# our kernels per layer step: route 3, dispatch gathers 2+1, dy dispatch 2, row
+# quantisations 3, grouped fwd 3 x 5, swiglu 1 + bwd 1, col quantisations 4,
+# wgrad 2 x 4, combine gather + combine 2
+EP_LAUNCHES_PER_STEP = 3 + 3 + 2 + 3 + 15 + 2 + 4 + 8 + 2
+
+
+class EpLayerBench:
+    """One rank's share of the config-5 layer: resident tokens, routing,
+    gradients and its local experts."""
+
+    def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS):
+        m = pkg()
+        W = m.workloads
+        dev = torch.device("cuda", torch.cuda.current_device())
+        logp = W.zipf_log_popularity(EP_EXPERTS, EP_ZIPF, seed)
+        ids = W.zipf_topk_sample(tokens, logp, EP_TOPK, seed=seed * 7919 + 1 + rank)
+        slot = None
+        if placement == "balanced" and world > 1:
+            slot = m.ep.balanced_placement(W.expected_expert_load(logp, EP_TOPK), world)
+        self.placement = placement if world > 1 else "single"
+        self.ep = m.ExpertParallel(EP_EXPERTS, placement=slot)
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + 17 + rank)
+        self.x = torch.randn(tokens, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16)
+        self.dy = (torch.randn(tokens, HIDDEN, generator=g, device=dev) * 1e-2).to(torch.bfloat16)
+        self.ids = torch.from_numpy(ids).to(dev)
+        p = torch.rand(tokens, EP_TOPK, generator=g, device=dev) + 0.1
+        self.probs = p / p.sum(1, keepdim=True)
+        e_loc = self.ep.e_local
+        w_gu = torch.randn(e_loc, GATE_UP, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
+        w_d = torch.randn(e_loc, HIDDEN, INTER, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
+        self.comm = torch.cuda.Stream() if (overlap and world > 1) else None
+        self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm)
+        del w_gu, w_d
+        torch.cuda.synchronize()
+
+    def step(self, x=None, ids=None, probs=None, dy=None):
+        return self.layer.step(self.x if x is None else x, self.ids if ids is None else ids,
+                               self.probs if probs is None else probs, self.dy if dy is None else dy)
+
+
+def time_ep_layer(lb, steps, warmup, world):
+    """Events on the main stream around K layer steps (the comm stream joins
+    the main stream inside every step), plus per-segment marks."""
+    for _ in range(warmup):
+        out = lb.step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    lb.layer.marks = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        out, dw_gu, dw_d, plan = lb.step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    seg = {}
+    marks = lb.layer.marks
+    lb.layer.marks = None
+    for (a, ea), (b, eb) in zip(marks, marks[1:]):
+        if b == "start":
+            continue
+        seg[b] = seg.get(b, 0.0) + ea.elapsed_time(eb) / steps
+    return ms, seg, plan
+
+
+def e2e_ep_layer(lb, steps):
+    """Through the public API with host buffers: pinned x, dy, expert ids and
+    router probs -> H2D -> layer step -> D2H of the combined output."""
+    dev = lb.x.device
+    host = {k: torch.empty(getattr(lb, k).shape, dtype=getattr(lb, k).dtype, pin_memory=True)
+            for k in ("x", "ids", "probs", "dy")}
+    for k, h in host.items():
+        h.copy_(getattr(lb, k))
+    out_h = torch.empty(lb.x.shape, dtype=torch.bfloat16, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_h.numel() * out_h.element_size()
+
+    def step():
+        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        out, _, _, _ = lb.step(d["x"], d["ids"], d["probs"], d["dy"])
+        out_h.copy_(out, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps, h2d, d2h
+
+
+def sum_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([float(v)], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+def gather_over_ranks(v, world):
+    if world == 1:
+        return [v]
+    t = torch.tensor([float(v)], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
+def measure_ep_layer(lb, world, steps, warmup):
+    """Timed config-5 layer steps on this process group (every rank takes the
+    same collective steps)."""
+    ms, seg, plan = time_ep_layer(lb, steps, warmup, world)
+    code = pkg().device_error()
+    if code:
+        raise RuntimeError(f"device error {code} during the EP layer timed region")
+    ms_max = max_over_ranks(ms, world)
+    flops = lb.layer.gemm_flops(plan)
+    flops_all = sum_over_ranks(sum(flops.values()), world)
+    rows = gather_over_ranks(plan.recv_rows, world)
+    pk = peaks()
+    gemm_ms = {k: seg[k] for k in flops}
+    dom = max(gemm_ms, key=lambda k: gemm_ms[k])
+    achieved = flops[dom] / (gemm_ms[dom] * 1e-3) / 1e12
+    return {"value": flops_all / (ms_max * 1e-3) / 1e12, "ms_per_step": ms_max,
+            "ms_per_step_this_rank": ms, "flops_per_step_all_ranks": flops_all,
+            "recv_rows_per_rank": {"max": max(rows), "mean": sum(rows) / len(rows), "min": min(rows)},
+            "padded_rows_this_rank": int(sum(plan.group_rows_host)),
+            "segments_ms_rank0": {k: round(v, 4) for k, v in seg.items()},
+            "gemm_tflops_rank0": {k: round(flops[k] / (gemm_ms[k] * 1e-3) / 1e12, 1) for k in flops},
+            "roofline": {"bound": "tensor", "kernel": f"grouped_gemm_kernel ({dom}, EP layer)",
+                         "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
+                         "peak_source": pk["source"], "traffic": None,
+                         "flops_per_launch": flops[dom]},
+            "placement": lb.placement, "overlap": lb.comm is not None}
+
+
+def run_ep_mxg(args, rank, world, local):
+    """The N>1 bench line: config 5 across the process group."""
+    pkg()._lib.load()
+    lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=not args.no_overlap)
+    with ClockSampler(local) as clk:
+        r = measure_ep_layer(lb, world, args.steps, args.warmup)
+    e2e = None
+    if not args.no_e2e:
+        e_ms, h2d, d2h = e2e_ep_layer(lb, max(2, min(5, args.steps)))
+        e_ms = max_over_ranks(e_ms, world)
+        e2e = {"value": round(r["flops_per_step_all_ranks"] / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3)}
+    out = {"metric": METRIC, "value": round(r["value"], 2), "unit": "TFLOPS", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
+           "data": "synthetic",
+           "config": {"workload": "dsv3_ep_layer (config 5): dispatch, quantize, gate/up fwd, swiglu, "
+                                  "down fwd, combine + down dgrad and both wgrads",
+                      "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
+                      "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
+                      "hidden": HIDDEN, "intermediate": INTER, "placement": r["placement"],
+                      "comm_overlap": r["overlap"], "parallelism": f"ep{world}",
+                      "l2": "operands > L2 (no flush needed)"},
+           "roofline": r["roofline"], "layer": {k: r[k] for k in (
+               "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
+               "padded_rows_this_rank", "segments_ms_rank0", "gemm_tflops_rank0")},
+           "cpu_baseline": None, "e2e": e2e,
+           "gpu_launches": args.steps * EP_LAUNCHES_PER_STEP, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
 # ---------------------------------------------------------------- arms
 def traffic_from_profiles():
     path = os.path.join(REPO, "profiles", "ncu_traffic.json")
@@ -447,7 +629,7 @@ def run_mxg(args, rank, world, local):
            "data": "synthetic",
            "config": {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)"
                       if args.case == "dsv3" else "small profiling case (8 experts, 16384 rows)",
-                      "experts_per_gpu": E, "hidden": HIDDEN, "intermediate": INTER,
+                      "experts_per_gpu": wl.E, "hidden": HIDDEN, "intermediate": INTER,
                       "routed_rows_per_gpu": wl.split.real_rows, "padded_rows": wl.M,
                       "routing": "multinomial over Dirichlet(1.0), groups padded to 32",
                       "flops_per_step_per_gpu": flops_step, "l2": "operands > L2 (no flush needed)",
@@ -455,13 +637,100 @@ def run_mxg(args, rank, world, local):
            "roofline": roofline, "quantize": quant, "cpu_baseline": cpu, "e2e": e2e,
            "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.values()),
            "clocks": clk.summary()}
+    if not args.no_ep and args.case == "dsv3":
+        del wl, calls
+        torch.cuda.empty_cache()
+        lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=False)
+        r = measure_ep_layer(lb, world, min(args.steps, 50), args.warmup)
+        del lb
+        out["ep_layer_1gpu"] = {"value": round(r["value"], 2), "unit": "TFLOPS",
+                                "ms_per_step": round(r["ms_per_step"], 4),
+                                "note": "config 5 layer on one GPU (all 256 experts, 16384 tokens): "
+                                        "the same per-GPU work as each rank of the N>1 lines",
+                                "gemm_tflops": r["gemm_tflops_rank0"],
+                                "segments_ms": r["segments_ms_rank0"],
+                                "recv_rows": r["recv_rows_per_rank"]["max"]}
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def cpu_reference_layer_sample(host, threads):
+    """The reference's torch path for the five GEMMs of the config-5 layer on
+    the host (dequantise in fp32, fp32 matmul), for the sampled experts."""
+    from oracle import mxfp8_oracle as orc
+    torch.set_num_threads(threads)
+    deq = orc.dequantize_torch
+    flops = 0
+    t0 = time.perf_counter()
+    for e in host:
+        r = e["rows"]
+        x = deq(e["xq"], e["xs"])
+        _ = x @ deq(e["wgu"], e["wgus"]).T                    # gate/up fwd  [r, 4096]
+        _ = deq(e["hq"], e["hs"]) @ deq(e["wd"], e["wds"]).T  # down fwd     [r, 7168]
+        dy = deq(e["dyq"], e["dys"])
+        _ = dy @ deq(e["wdt"], e["wdts"]).T                   # down dgrad   [r, 2048]
+        _ = deq(e["go_d"], e["gos_d"]) @ deq(e["ia_d"], e["ias_d"]).T   # down wgrad
+        _ = deq(e["go_g"], e["gos_g"]) @ deq(e["ia_g"], e["ias_g"]).T   # gate/up wgrad
+        flops += 14 * r * HIDDEN * INTER
+    return flops, time.perf_counter() - t0
+
+
+def run_reference_layer(args, world):
+    """Reference arm at N>1: the config-5 layer's GEMMs on the host for the
+    two median-loaded experts (rows as the routing sends them per step)."""
+    m = pkg()
+    threads = os.cpu_count() or 1
+    logp = m.workloads.zipf_log_popularity(EP_EXPERTS, EP_ZIPF, args.seed)
+    rows_e = m.workloads.expected_expert_load(logp, EP_TOPK) * EP_TOKENS * world
+    order = np.argsort(rows_e)
+    experts = [int(i) for i in order[len(order) // 2 - 1: len(order) // 2 + 1]]
+    g = torch.Generator().manual_seed(args.seed)
+    rnd = lambda *s: torch.randint(0, 126, s, generator=g, dtype=torch.uint8)
+    sc = lambda *s: torch.randint(118, 128, s, generator=g, dtype=torch.uint8)
+    host = []
+    for e in experts:
+        r = int(-(-int(round(rows_e[e])) // 32) * 32)
+        host.append({"rows": r, "xq": rnd(r, HIDDEN), "xs": sc(r, HIDDEN // 32),
+                     "wgu": rnd(GATE_UP, HIDDEN), "wgus": sc(GATE_UP, HIDDEN // 32),
+                     "hq": rnd(r, INTER), "hs": sc(r, INTER // 32),
+                     "wd": rnd(HIDDEN, INTER), "wds": sc(HIDDEN, INTER // 32),
+                     "dyq": rnd(r, HIDDEN), "dys": sc(r, HIDDEN // 32),
+                     "wdt": rnd(INTER, HIDDEN), "wdts": sc(INTER, HIDDEN // 32),
+                     "go_d": rnd(HIDDEN, r), "gos_d": sc(HIDDEN, r // 32),
+                     "ia_d": rnd(INTER, r), "ias_d": sc(INTER, r // 32),
+                     "go_g": rnd(GATE_UP, r), "gos_g": sc(GATE_UP, r // 32),
+                     "ia_g": rnd(HIDDEN, r), "ias_g": sc(HIDDEN, r // 32)})
+    for _ in range(args.warmup):
+        cpu_reference_layer_sample(host, threads)
+    tot_fl, tot_dt = 0, 0.0
+    for _ in range(args.steps):
+        fl, dt = cpu_reference_layer_sample(host, threads)
+        tot_fl += fl
+        tot_dt += dt
+    v = tot_fl / tot_dt / 1e12
+    sample = (f"per step experts {experts} ({[h['rows'] for h in host]} rows) of the config-5 layer: "
+              "gate/up fwd, down fwd, down dgrad, both wgrads; torch fp32 dequantise+matmul "
+              "(reference fused_fwd.py:249-264, scale_correctness.py:110-137); no all-to-all (one host)")
+    out = {"metric": METRIC, "value": round(v, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(1e3 * tot_dt / args.steps, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic", "impl": "reference",
+           "config": {"workload": "dsv3_ep_layer (config 5) GEMMs, CPU sample",
+                      "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
+                      "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "hidden": HIDDEN,
+                      "intermediate": INTER, "parallelism": f"ep{world}"},
+           "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
+                            "kind": "port", "sample": sample},
+           "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
 
 
 def run_reference(args, rank, world, local):
     """Reference arm: the reference's CPU torch path, rank 0 only."""
     if rank != 0:
+        return
+    if world > 1:
+        run_reference_layer(args, world)
         return
     m = pkg()
     from oracle import mxfp8_oracle as orc  # noqa: F401  (the checker, used as the timed CPU port)
@@ -519,6 +788,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--case", default="dsv3", choices=["dsv3", "small"],
                     help="small: reduced problem for profiler captures (not a bench line)")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert placement for the EP layer (N>1)")
+    ap.add_argument("--no-overlap", action="store_true", help="EP layer: collectives on the main stream")
+    ap.add_argument("--no-ep", action="store_true", help="N=1: skip the one-GPU EP layer measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -527,7 +800,10 @@ def main():
         return
     rank, world, local = dist_init(args.gpus)
     try:
-        run_mxg(args, rank, world, local)
+        if world > 1:
+            run_ep_mxg(args, rank, world, local)
+        else:
+            run_mxg(args, rank, world, local)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -165,6 +165,50 @@ MXG_API int mxg_grouped_wgrad_run(const void* go, const void* ia, int num_groups
                                   int64_t n, int64_t k, void* out, int out_dtype, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* ---- expert parallelism: token routing (experts sharded evenly over ranks) ----
+ * Global expert e lives on rank e / E_local as local expert e % E_local.  The
+ * reference relies on torchtitan's MoE token dispatcher for this step
+ * (port_mxfp8.py:74,214-218,240: all-to-all dispatch, groups padded to 32). */
+#define MXG_EP_MAX_EXPERTS 384
+#define MXG_EP_MAX_RANKS 64
+
+/* Stable counting sort of routing slots (token t, choice j at t*topk + j) by
+ * expert slot = slot_of_expert[expert id] (slot_of_expert null = identity;
+ * slot s lives on rank s / E_local): counts[s], send_rows[p] = token row sent
+ * at position p (positions grouped by slot, tokens in order),
+ * slot_pos[t*topk+j] = p.  An id outside [0, num_experts) sets the device
+ * error word to MXG_ERR_INVALID_ARGUMENT and its slot_pos to -1. */
+MXG_API size_t mxg_ep_route_workspace_size(int64_t n_slots, int num_experts);
+MXG_API int mxg_ep_route(const int32_t* expert_ids, const int32_t* slot_of_expert, int64_t n_slots,
+                         int topk, int num_experts, int32_t* counts, int32_t* send_rows,
+                         int32_t* slot_pos, void* workspace, size_t workspace_bytes, void* stream);
+
+/* dst[i] = src[idx[i]] for rows of row_bytes (multiple of 16); idx[i] < 0 or
+ * >= src_rows gives a zero row. */
+MXG_API int mxg_gather_rows(const void* src, int64_t src_rows, int64_t row_bytes, const int32_t* idx,
+                            int64_t n, void* dst, void* stream);
+
+/* Rows received from every rank (ordered by source rank, then local expert,
+ * counts in recv_counts[world][e_local]) -> expert-major groups padded to
+ * `pad` rows: idx[i] = received row of padded row i (-1 for padding),
+ * back[received row] = its padded row, group_rows[le] = padded group size. */
+MXG_API int mxg_ep_regroup(const int32_t* recv_counts, int world, int e_local, int pad, int32_t* idx,
+                           int32_t* back, int32_t* group_rows, void* stream);
+
+/* out[t] = sum_j w[t*topk+j] * rows[slot_pos[t*topk+j]] (bf16 rows, fp32 sum,
+ * bf16 out; weights may be null = 1). */
+MXG_API int mxg_ep_combine(const void* rows, const int32_t* slot_pos, const float* weights,
+                           int64_t n_tokens, int topk, int64_t hidden, void* out, void* stream);
+
+/* h = silu(g) * u for gu rows [g (inter) | u (inter)], bf16 (the gate/up ->
+ * down activation of the expert FFN, e2e_bench.py:56-61). */
+MXG_API int mxg_swiglu(const void* gu, int64_t rows, int64_t inter, void* h, void* stream);
+
+/* Backward of mxg_swiglu: dgu = [dg | du] (bf16 [rows, 2*inter]) from gu and
+ * dh (bf16 [rows, inter]). */
+MXG_API int mxg_swiglu_bwd(const void* gu, const void* dh, int64_t rows, int64_t inter, void* dgu,
+                           void* stream);
+
 /* ---- byte transpose: dst [cols, rows] = src [rows, cols]^T (uint8) ----------- */
 MXG_API int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, void* dst, void* stream);
 

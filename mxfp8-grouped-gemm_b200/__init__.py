@@ -5,7 +5,8 @@ directory name is not a Python identifier) after putting the repository root
 on ``sys.path``.  The compute runs in ``libmxg.so`` (C ABI, ``include/mxg.h``);
 build it with ``python mxfp8-grouped-gemm_b200/build.py``.
 """
-from . import _lib, ops, workloads
+from . import _lib, ep, moe, ops, workloads
+from .ep import ExpertParallel
 from ._lib import MxgError, device_error, raise_device_error
 from .fused_fwd import fused_grouped_fwd, reference_grouped_gemm
 from .fwd_final import fwd_ge
@@ -16,5 +17,5 @@ __all__ = [
     "fused_grouped_fwd", "reference_grouped_gemm", "fwd_ge",
     "wgrad_fused", "wgrad_prepare", "wgrad_kernel",
     "quantize_rowwise", "quantize_colwise", "to_mxfp8_dim0", "to_mxfp8_dim1",
-    "MxgError", "device_error", "raise_device_error", "ops", "workloads",
+    "ExpertParallel", "MxgError", "device_error", "raise_device_error", "ep", "moe", "ops", "workloads",
 ]

@@ -51,6 +51,13 @@ _PROTOS = {
     "mxg_grouped_wgrad": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
                                    _c_i64, _vp, _c_int, _vp, _c_size, _vp]),
     "mxg_transpose_u8": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
+    "mxg_ep_route_workspace_size": (_c_size, [_c_i64, _c_int]),
+    "mxg_ep_route": (_c_int, [_vp, _vp, _c_i64, _c_int, _c_int, _vp, _vp, _vp, _vp, _c_size, _vp]),
+    "mxg_gather_rows": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp]),
+    "mxg_ep_regroup": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp]),
+    "mxg_ep_combine": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_i64, _vp, _vp]),
+    "mxg_swiglu": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
+    "mxg_swiglu_bwd": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "mxg_debug_inject_stall": (_c_int, [_c_i64]),
 }
 

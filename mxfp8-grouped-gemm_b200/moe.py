@@ -1,0 +1,127 @@
+"""MoE expert FFN over expert parallelism on the MXFP8 grouped GEMMs.
+
+The layer the reference trains with (``e2e_bench.py:56-61,91-108``: gate/up
+projection, SiLU-gated product, down projection per expert, under torchtitan's
+token dispatcher with MXFP8 grouped GEMMs patched in, ``port_mxfp8.py:175-194``)
+built from this library's pieces:
+
+forward   dispatch x -> quantize 1x32 -> gate/up grouped fwd -> swiglu ->
+          quantize -> down grouped fwd -> combine (weighted by router probs)
+backward  dispatch dy along the same plan -> quantize -> down dgrad (grouped
+          fwd against the pre-quantised transposed down weights) -> swiglu
+          backward -> 32x1 quantisations -> down and gate/up weight gradients
+
+Weights are quantised once (static between optimiser steps).  With a comm
+stream the dy dispatch runs under the forward GEMMs and the combine under the
+backward GEMMs; only the x dispatch (and its count exchange) sits in front of
+the first GEMM.  The activation gradient of the gate/up projection (dx) is not
+computed: the benchmark layer step covers the forward and both weight
+gradients.
+"""
+from __future__ import annotations
+
+from contextlib import nullcontext
+
+import torch
+
+from . import _lib, ops
+from .ep import ExpertParallel
+
+
+class ExpertFFN:
+    """Local experts of one rank: w_gate_up [E_local, 2I, H] and w_down
+    [E_local, H, I] bf16 (quantised here once)."""
+
+    def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
+                 comm_stream: torch.cuda.Stream | None = None):
+        self.ep = ep
+        E, I2, H = w_gate_up.shape
+        E2, H2, I = w_down.shape
+        if E != ep.e_local or E2 != E or H2 != H or I2 != 2 * I:
+            raise ValueError("weights must be [E_local, 2I, H] and [E_local, H, I]")
+        self.E, self.H, self.I = E, H, I
+        q, s = ops.quantize_rowwise(w_gate_up.reshape(E * 2 * I, H))
+        self.wgu = (q.view(E, 2 * I, H), s.view(E, 2 * I, H // 32))
+        q, s = ops.quantize_rowwise(w_down.reshape(E * H, I))
+        self.wd = (q.view(E, H, I), s.view(E, H, I // 32))
+        wdt = w_down.transpose(1, 2).contiguous()            # [E, I, H] for dh = dy . W_d
+        q, s = ops.quantize_rowwise(wdt.view(E * I, H))
+        self.wdt = (q.view(E, I, H), s.view(E, I, H // 32))
+        del wdt
+        self.comm = comm_stream
+        self.marks = None           # optional list of (name, cuda event) for profiling
+
+    def _mark(self, name):
+        if self.marks is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.marks.append((name, e))
+
+    def _fwd(self, a, w, offs, out_dtype=torch.bfloat16):
+        q, s = a
+        wq, ws = w
+        return ops.grouped_fwd(q, wq, offs, s, ws, out_dtype=out_dtype, offs_kind=_lib.OFFS_SIZES)
+
+    def _wgrad(self, go, ia, offs):
+        return ops.grouped_wgrad(go[0], ia[0], offs, go[1], ia[1], out_dtype=torch.float32,
+                                 offs_kind=_lib.OFFS_SIZES, num_groups=self.E)
+
+    def step(self, x, expert_ids, probs, dy):
+        """Forward and weight gradients of one layer step.  x, dy [n, H] bf16,
+        expert_ids [n, k] int32, probs [n, k] fp32.  Returns (out [n, H] bf16,
+        dW_gate_up [E_local, 2I, H] fp32, dW_down [E_local, H, I] fp32, plan)."""
+        ep = self.ep
+        main = torch.cuda.current_stream()
+        comm = self.comm
+        side = (lambda: torch.cuda.stream(comm)) if comm is not None else nullcontext
+        self._mark("start")
+        x_local, plan = ep.dispatch(x, expert_ids)
+        offs = plan.group_rows
+        self._mark("dispatch")
+        if comm is not None:
+            comm.wait_stream(main)
+        with side():
+            dy_local = ep.dispatch_like(dy, plan)
+            dy_ready = torch.cuda.Event()
+            dy_ready.record()
+        xq = ops.quantize_rowwise(x_local)
+        self._mark("quantize_x")
+        gu = self._fwd(xq, self.wgu, offs)
+        self._mark("fwd_gate_up")
+        h = ops.swiglu(gu)
+        hq = ops.quantize_rowwise(h)
+        self._mark("swiglu_quantize_h")
+        y_local = self._fwd(hq, self.wd, offs)
+        self._mark("fwd_down")
+        if comm is not None:
+            comm.wait_stream(main)
+        with side():
+            out = ep.combine(y_local, plan, probs)
+        main.wait_event(dy_ready)
+        dyq = ops.quantize_rowwise(dy_local)
+        self._mark("quantize_dy")
+        dh = self._fwd(dyq, self.wdt, offs)
+        self._mark("dgrad_down")
+        dgu = ops.swiglu_bwd(gu, dh)
+        go_d, ia_d = ops.quantize_colwise(dy_local), ops.quantize_colwise(h)
+        self._mark("swiglu_bwd_quantize_down")
+        dw_d = self._wgrad(go_d, ia_d, offs)
+        self._mark("wgrad_down")
+        go_g, ia_g = ops.quantize_colwise(dgu), ops.quantize_colwise(x_local)
+        self._mark("quantize_gate_up")
+        dw_gu = self._wgrad(go_g, ia_g, offs)
+        self._mark("wgrad_gate_up")
+        if comm is not None:
+            # Every later use of memory from either stream is ordered after
+            # this wait (the next dispatch syncs on main before the comm
+            # stream waits on main), so no record_stream is needed.
+            main.wait_stream(comm)
+        self._mark("combine")
+        return out, dw_gu, dw_d, plan
+
+    def gemm_flops(self, plan) -> dict:
+        """Algorithmic FLOPs of the step's five grouped GEMMs on real rows."""
+        r, H, I = plan.recv_rows, self.H, self.I
+        return {"fwd_gate_up": 2 * r * 2 * I * H, "fwd_down": 2 * r * H * I,
+                "dgrad_down": 2 * r * I * H, "wgrad_down": 2 * r * H * I,
+                "wgrad_gate_up": 2 * r * 2 * I * H}

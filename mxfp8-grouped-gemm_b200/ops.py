@@ -171,6 +171,35 @@ def transpose_u8(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """h = silu(g) * u for bf16 rows gu = [g | u] ([R, 2I] -> [R, I]); the
+    activation between the gate/up and down projections of an expert."""
+    _cuda(gu, "gu")
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2 or gu.shape[1] % 2:
+        raise ValueError("swiglu takes a [R, 2I] bf16 tensor")
+    gu = gu.contiguous()
+    R, I2 = gu.shape
+    h = torch.empty(R, I2 // 2, dtype=torch.bfloat16, device=gu.device)
+    _lib.check(_lib.load().mxg_swiglu(gu.data_ptr(), R, I2 // 2, h.data_ptr(),
+                                      _lib.stream_ptr(gu.device)), "mxg_swiglu")
+    return h
+
+
+def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    """Gradient of ``swiglu`` w.r.t. gu = [g | u]: bf16 [R, 2I] from dh [R, I]."""
+    _cuda(gu, "gu")
+    _cuda(dh, "dh")
+    if gu.dtype != torch.bfloat16 or dh.dtype != torch.bfloat16 or gu.dim() != 2 \
+            or dh.shape != (gu.shape[0], gu.shape[1] // 2) or gu.shape[1] % 2:
+        raise ValueError("swiglu_bwd takes gu [R, 2I] and dh [R, I], both bf16")
+    gu, dh = gu.contiguous(), dh.contiguous()
+    dgu = torch.empty_like(gu)
+    _lib.check(_lib.load().mxg_swiglu_bwd(gu.data_ptr(), dh.data_ptr(), gu.shape[0], dh.shape[1],
+                                          dgu.data_ptr(), _lib.stream_ptr(gu.device)),
+               "mxg_swiglu_bwd")
+    return dgu
+
+
 # ---------------------------------------------------------------- two-phase plans
 class GroupedFwdPlan:
     """Groups and packed scales of one grouped forward, prepared once in a

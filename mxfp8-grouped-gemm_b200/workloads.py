@@ -90,6 +90,31 @@ def zipf_topk_assign(num_tokens, num_experts=256, topk=8, s=1.1, seed=0) -> np.n
     return np.argpartition(-(logp[None, :] + g), topk - 1, axis=1)[:, :topk].astype(np.int64)
 
 
+def zipf_log_popularity(num_experts=256, s=1.1, seed=0) -> np.ndarray:
+    """log popularity of each expert, 1/rank^s over a seeded random ranking
+    (shared by every rank of an expert-parallel group)."""
+    ranks = np.random.default_rng(seed).permutation(num_experts) + 1
+    return -s * np.log(ranks.astype(np.float64))
+
+
+def zipf_topk_sample(num_tokens, logp, topk=8, seed=0) -> np.ndarray:
+    """[num_tokens, topk] distinct experts per token drawn with popularity
+    exp(logp) (Gumbel top-k, without replacement), in the token's own order of
+    preference."""
+    g = np.random.default_rng(seed).gumbel(size=(num_tokens, logp.size))
+    score = logp[None, :] + g
+    part = np.argpartition(-score, topk - 1, axis=1)[:, :topk]
+    order = np.argsort(-np.take_along_axis(score, part, axis=1), axis=1)
+    return np.take_along_axis(part, order, axis=1).astype(np.int32)
+
+
+def expected_expert_load(logp, topk=8, samples=65536, seed=12345) -> np.ndarray:
+    """Expected routed rows per expert per token (a fixed calibration sample of
+    the same top-k sampler); used for load-aware expert placement."""
+    ids = zipf_topk_sample(samples, logp, topk, seed)
+    return np.bincount(ids.reshape(-1), minlength=logp.size) / samples
+
+
 # ---------------------------------------------------------------- problem shapes
 @dataclass
 class FwdShape:

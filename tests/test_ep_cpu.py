@@ -1,0 +1,136 @@
+"""Expert-parallel dispatch/combine on CPU: the oracle's routing pieces against
+brute force, and ``ExpertParallel``'s orchestration over a world-size-2
+``gloo`` process group with the oracle's pieces injected as its ops."""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from ep_support import OracleEpOps, free_port, make_rank_inputs
+from oracle import ep_oracle
+
+
+def test_route_is_stable_counting_sort():
+    ids, _, _ = make_rank_inputs(0, 200, 8, 64, 16, zipf=1.1)
+    counts, send_rows, slot_pos = ep_oracle.route(ids, 64)
+    assert counts.sum() == ids.size
+    # brute force: walk experts in order, slots in (t, j) order
+    want = [t for e in range(64) for t in range(ids.shape[0]) for j in range(8) if ids[t, j] == e]
+    assert send_rows.tolist() == want
+    flat = ids.reshape(-1)
+    assert np.all(flat[np.argsort(slot_pos)] == np.sort(flat, kind="stable"))
+    assert np.all(send_rows[slot_pos] == np.arange(ids.size) // 8)
+
+
+def test_regroup_pads_expert_major():
+    rc = np.array([[3, 0, 33], [1, 0, 0], [0, 0, 31]], dtype=np.int32)  # 3 ranks x 3 experts
+    idx, back, gr = ep_oracle.regroup(rc, 32)
+    assert gr.tolist() == [32, 0, 64]
+    # received order: r0e0(0..2) r0e2(3..35) r1e0(36) r2e2(37..67)
+    assert idx[:4].tolist() == [0, 1, 2, 36] and np.all(idx[4:32] == -1)
+    assert idx[32:65].tolist() == list(range(3, 36)) and idx[65:96].tolist() == list(range(37, 68))
+    assert np.all(idx[back] == np.arange(back.size))
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_simulated_dispatch_combine_roundtrip(world):
+    E, k, H = 16, 4, 32
+    xs, ids, ws, ns = [], [], [], []
+    for r in range(world):
+        n = [37, 0, 64, 5][r]
+        i, x, w = make_rank_inputs(r, n, k, E, H, zipf=1.1)
+        xs.append(x), ids.append(i), ws.append(w), ns.append(n)
+    out, routed, send_counts = ep_oracle.simulate(xs, ids, E)
+    for d, (xl, rc, plan) in enumerate(out):
+        assert xl.shape[0] == plan["group_rows"].sum() and xl.shape[0] % 32 == 0
+        e_loc = E // world
+        # every non-pad row of local expert le comes from a token routed to it
+        starts = np.concatenate([[0], np.cumsum(plan["group_rows"])])
+        for le in range(e_loc):
+            rows = xl[starts[le]:starts[le + 1]]
+            real = int(rc[:, le].sum())
+            assert np.all(rows[real:] == 0)
+            ge = d * e_loc + le
+            srcs = np.concatenate([xs[s][np.nonzero((ids[s] == ge).any(1))[0]] for s in range(world)])
+            assert np.array_equal(rows[:real], srcs)
+    ys = [o[0] * 2.0 for o in out]
+    back = ep_oracle.simulate_combine(ys, routed, send_counts, [o[2] for o in out], ws, ns, k)
+    for s in range(world):
+        np.testing.assert_allclose(back[s], 2.0 * ws[s].sum(1, keepdims=True) * xs[s], rtol=1e-5, atol=1e-5)
+
+
+def test_balanced_placement_even_and_balanced():
+    from conftest import load_pkg
+    ep = load_pkg().ep
+    W = load_pkg().workloads
+    ids = W.zipf_topk_assign(32768, 256, 8, 1.1, seed=0)
+    load = np.bincount(ids.reshape(-1), minlength=256)
+    for world in (2, 4, 8):
+        slot = ep.balanced_placement(load, world)
+        assert np.array_equal(np.sort(slot), np.arange(256))
+        per_rank = np.zeros(world)
+        np.add.at(per_rank, slot // (256 // world), load)
+        contiguous = load.reshape(world, -1).sum(1)
+        assert per_rank.max() / per_rank.mean() <= 1.03
+        assert per_rank.max() <= contiguous.max()
+
+
+def test_route_with_placement_matches_permuted_ids():
+    ids, _, _ = make_rank_inputs(0, 300, 4, 16, 8, zipf=1.1)
+    perm = np.random.default_rng(1).permutation(16).astype(np.int32)
+    a = ep_oracle.route(ids, 16, perm)
+    b = ep_oracle.route(perm[ids], 16)
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v)
+
+
+def _gloo_worker(rank, world, port, q, balanced=False):
+    try:
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from conftest import load_pkg
+        ep = load_pkg().ep
+        E, k, H = 8, 2, 64
+        ns = [48, 0] if world == 2 else [48]
+        slot = ep.balanced_placement(np.arange(E)[::-1] ** 2, world) if balanced else None
+        par = ep.ExpertParallel(E, ops=OracleEpOps(), placement=slot)
+        ids, x, w = make_rank_inputs(rank, ns[rank], k, E, H, zipf=1.2)
+        xb = torch.from_numpy(x).to(torch.bfloat16)
+        x_local, plan = par.dispatch(xb, torch.from_numpy(ids))
+        # oracle over all ranks' inputs
+        all_in = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.2) for r in range(world)]
+        xs = [torch.from_numpy(a[1]).to(torch.bfloat16).float().numpy() for a in all_in]
+        out, routed, sc = ep_oracle.simulate(xs, [a[0] for a in all_in], E, slot_of_expert=slot)
+        assert np.array_equal(x_local.float().numpy(), out[rank][0]), "dispatch rows"
+        again = par.dispatch_like(xb * 2, plan)
+        assert np.array_equal(again.float().numpy(), 2 * out[rank][0]), "dispatch_like rows"
+        assert plan.group_rows_host == out[rank][2]["group_rows"].tolist()
+        y = combined = par.combine(x_local, plan, torch.from_numpy(w))
+        want = ep_oracle.simulate_combine([o[0] for o in out], routed, sc, [o[2] for o in out],
+                                          [a[2] for a in all_in], ns, k)[rank]
+        np.testing.assert_allclose(y.float().numpy(), want, rtol=1e-2, atol=1e-2)
+        assert combined.shape == (ns[rank], H)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # report to the parent
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,balanced", [(1, False), (2, False), (2, True)])
+def test_expert_parallel_gloo(world, balanced):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, q, balanced)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert res[r] == "ok", res[r]

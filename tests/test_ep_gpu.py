@@ -1,0 +1,217 @@
+"""Expert-parallel routing kernels vs the oracle (bit-exact for the integer
+maps and row moves; the weighted combine within one bf16 ulp of the oracle's
+fp32 sum; swiglu within 1e-2 relative of a torch fp32 reference), one expert
+layer through dispatch -> MXFP8 GEMMs -> combine against fp64, and a
+world-size-2 NCCL dispatch/combine when the box has two GPUs."""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from ep_support import free_port, make_rank_inputs
+from oracle import ep_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16(x, dev):
+    return torch.from_numpy(np.asarray(x, np.float32)).to(torch.bfloat16).to(dev)
+
+
+def combine_close(got, rows, slot_pos, w, n, k):
+    """got within one bf16 ulp of the oracle's fp32 weighted sum, plus the
+    fp32 rounding of the k-term sum (FMA vs multiply-then-add) relative to the
+    sum of magnitudes, which dominates where the terms cancel."""
+    want = ep_oracle.combine(rows, slot_pos, w, n, k)
+    mag = ep_oracle.combine(np.abs(rows), slot_pos, None if w is None else np.abs(w), n, k)
+    return bool(np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -7 + mag * 2.0 ** -20))
+
+
+@pytest.mark.parametrize("n,k,E,zipf", [(0, 8, 256, None), (1, 1, 4, None), (1000, 2, 8, 1.2),
+                                        (16384, 8, 256, 1.1), (3000, 8, 384, 1.1), (5000, 4, 32, None)])
+def test_route_bit_exact(mxg, cuda_dev, n, k, E, zipf):
+    ids, _, _ = make_rank_inputs(0, n, k, E, 16, seed=n, zipf=zipf)
+    ops = mxg.ep.CudaEpOps()
+    c, sr, sp = ops.route(torch.from_numpy(ids).to(cuda_dev), E)
+    rc, rsr, rsp = ep_oracle.route(ids, E)
+    assert np.array_equal(c.cpu().numpy(), rc)
+    assert np.array_equal(sr.cpu().numpy(), rsr)
+    assert np.array_equal(sp.cpu().numpy(), rsp)
+    assert mxg.device_error() == 0
+
+
+def test_route_rejects_out_of_range_ids(mxg, cuda_dev):
+    ids = torch.tensor([[0, 9]], dtype=torch.int32, device=cuda_dev)
+    mxg.ep.CudaEpOps().route(ids, 8)
+    with pytest.raises(mxg.MxgError):
+        mxg.raise_device_error()
+
+
+@pytest.mark.parametrize("dtype,width", [(torch.bfloat16, 7168), (torch.uint8, 2048), (torch.bfloat16, 8)])
+def test_gather_rows_bit_exact(mxg, cuda_dev, dtype, width):
+    g = np.random.default_rng(3)
+    src = g.integers(0, 255, size=(300, width * (2 if dtype == torch.bfloat16 else 1)), dtype=np.uint8)
+    idx = g.integers(-3, 300, size=517).astype(np.int32)
+    s = torch.from_numpy(src).to(cuda_dev).view(dtype)
+    out = mxg.ep.CudaEpOps().gather(s, torch.from_numpy(idx).to(cuda_dev), idx.size)
+    want = ep_oracle.gather(src, idx, idx.size)
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("world,e_local", [(1, 32), (8, 32), (4, 1), (64, 6)])
+def test_regroup_bit_exact(mxg, cuda_dev, world, e_local):
+    g = np.random.default_rng(world * 100 + e_local)
+    rc = g.integers(0, 90, size=(world, e_local)).astype(np.int32)
+    rc[0, 0] = 0
+    if e_local > 1:
+        rc[:, 1] = 0          # an expert nobody routes to
+    idx, back, gr = ep_oracle.regroup(rc, 32)
+    d_idx, d_back, d_gr = mxg.ep.CudaEpOps().regroup(torch.from_numpy(rc).to(cuda_dev), 32,
+                                                     idx.size, back.size)
+    assert np.array_equal(d_idx.cpu().numpy(), idx)
+    assert np.array_equal(d_back.cpu().numpy(), back)
+    assert np.array_equal(d_gr.cpu().numpy(), gr)
+
+
+@pytest.mark.parametrize("n,k,H,weighted", [(513, 8, 7168, True), (64, 2, 4096, False), (0, 8, 64, True)])
+def test_combine_matches_oracle(mxg, cuda_dev, n, k, H, weighted):
+    g = np.random.default_rng(n + k)
+    rows = g.standard_normal((n * k, H)).astype(np.float32)
+    perm = g.permutation(n * k).astype(np.int32)
+    w = g.random((n, k)).astype(np.float32) if weighted else None
+    rb = _bf16(rows, cuda_dev)
+    out = mxg.ep.CudaEpOps().combine(rb, torch.from_numpy(perm).to(cuda_dev),
+                                     None if w is None else torch.from_numpy(w).to(cuda_dev), n, k)
+    assert combine_close(out.float().cpu().numpy(), rb.float().cpu().numpy(), perm, w, n, k)
+
+
+@pytest.mark.parametrize("R,I", [(1, 8), (4096, 2048), (777, 1536)])
+def test_swiglu(mxg, cuda_dev, R, I):
+    gen = torch.Generator(device=cuda_dev).manual_seed(R)
+    gu = (torch.randn(R, 2 * I, generator=gen, device=cuda_dev) * 3).to(torch.bfloat16)
+    h = mxg.ops.swiglu(gu)
+    g, u = gu.float()[:, :I], gu.float()[:, I:]
+    ref = torch.nn.functional.silu(g) * u
+    err = ((h.float() - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+    assert err <= 1e-2
+
+
+def test_expert_parallel_world1_matches_oracle(mxg, cuda_dev):
+    E, k, H, n = 16, 4, 512, 700
+    ids, x, w = make_rank_inputs(0, n, k, E, H, zipf=1.1)
+    par = mxg.ExpertParallel(E)
+    xb = _bf16(x, cuda_dev)
+    x_local, plan = par.dispatch(xb, torch.from_numpy(ids).to(cuda_dev))
+    out, routed, sc = ep_oracle.simulate([xb.float().cpu().numpy()], [ids], E)
+    assert np.array_equal(x_local.float().cpu().numpy(), out[0][0])
+    assert plan.group_rows_host == out[0][2]["group_rows"].tolist()
+    y = par.combine(x_local, plan, torch.from_numpy(w).to(cuda_dev))
+    # results return along the inverse path: row p of the send order is x[send_rows[p]]
+    rows = xb.float().cpu().numpy()[routed[0][1]]
+    assert combine_close(y.float().cpu().numpy(), rows, routed[0][2], w, n, k)
+
+
+def test_expert_layer_through_dispatch(mxg, orc, cuda_dev):
+    """dispatch -> rowwise quantize -> grouped fwd (offs = padded group sizes)
+    -> combine equals sum_j w_j * deq(x_t) @ deq(W_e).T, fp64 on the dequantised
+    operands, rel Frobenius <= 1e-3 against the oracle rounded as the path rounds."""
+    E, k, H, N, n = 8, 2, 256, 128, 300
+    ids, x, w = make_rank_inputs(0, n, k, E, H, zipf=1.1)
+    par = mxg.ExpertParallel(E)
+    xb = _bf16(x, cuda_dev)
+    x_local, plan = par.dispatch(xb, torch.from_numpy(ids).to(cuda_dev))
+    q, s = mxg.quantize_rowwise(x_local)
+    gen = torch.Generator(device=cuda_dev).manual_seed(5)
+    wb = (torch.randn(E, N, H, generator=gen, device=cuda_dev) * 0.05).to(torch.bfloat16)
+    wq, ws = mxg.quantize_rowwise(wb.view(E * N, H))
+    wq, ws = wq.view(E, N, H), ws.view(E, N, H // 32)
+    y_local = mxg.ops.grouped_fwd(q, wq, plan.group_rows, s, ws, out_dtype=torch.bfloat16, offs_kind=2)
+    out = par.combine(y_local, plan, torch.from_numpy(w).to(cuda_dev))
+    # oracle: per padded row fwd, then per-token weighted combine
+    qn, sn = q.view(torch.uint8).cpu().numpy(), s.cpu().numpy()
+    gr = np.array(plan.group_rows_host)
+    st = np.concatenate([[0], np.cumsum(gr)[:-1]])
+    ref_local = orc.round_to_bf16(orc.grouped_fwd(qn, sn, wq.view(torch.uint8).cpu().numpy(),
+                                                  ws.cpu().numpy(), st, st + gr))
+    routed = ep_oracle.route(ids, E)
+    back = plan.back.cpu().numpy()
+    want = ep_oracle.combine(ref_local[back], routed[2], w, n, k)
+    err = orc.rel_frobenius(out.float().cpu().numpy().astype(np.float64), want.astype(np.float64))
+    assert err <= 1e-2 and orc.rel_frobenius(y_local.float().cpu().numpy(), ref_local) <= 1e-3
+
+
+def _nccl_worker(rank, world, port, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from conftest import load_pkg
+        mxg = load_pkg()
+        dev = torch.device("cuda", rank)
+        E, k, H = 16, 8, 1024
+        ns = [2048, 512]
+        par = mxg.ExpertParallel(E)
+        all_in = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
+        ids, x, w = all_in[rank]
+        xb = _bf16(x, dev)
+        x_local, plan = par.dispatch(xb, torch.from_numpy(ids).to(dev))
+        xs = [torch.from_numpy(a[1]).to(torch.bfloat16).float().numpy() for a in all_in]
+        out, routed, sc = ep_oracle.simulate(xs, [a[0] for a in all_in], E)
+        ok = np.array_equal(x_local.float().cpu().numpy(), out[rank][0])
+        y = par.combine(x_local, plan, torch.from_numpy(w).to(dev))
+        rows = xs[rank][routed[rank][1]]
+        ok2 = combine_close(y.float().cpu().numpy(), rows, routed[rank][2], w, ns[rank], k)
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok" if ok and ok2 else f"dispatch {ok} combine {ok2}"))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+def test_expert_parallel_nccl_world2():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "ok", 1: "ok"}, res
+
+
+def test_route_with_placement_bit_exact(mxg, cuda_dev):
+    W = mxg.workloads
+    logp = W.zipf_log_popularity(256, 1.1, seed=0)
+    ids = W.zipf_topk_sample(16384, logp, 8, seed=1)
+    slot = mxg.ep.balanced_placement(W.expected_expert_load(logp, 8), 8)
+    c, sr, sp = mxg.ep.CudaEpOps().route(torch.from_numpy(ids).to(cuda_dev), 256,
+                                         torch.from_numpy(slot).to(cuda_dev))
+    rc, rsr, rsp = ep_oracle.route(ids, 256, slot)
+    assert np.array_equal(c.cpu().numpy(), rc)
+    assert np.array_equal(sr.cpu().numpy(), rsr)
+    assert np.array_equal(sp.cpu().numpy(), rsp)
+
+
+@pytest.mark.parametrize("R,I", [(1, 8), (4096, 2048), (333, 1536)])
+def test_swiglu_bwd_matches_autograd(mxg, cuda_dev, R, I):
+    gen = torch.Generator(device=cuda_dev).manual_seed(R + 1)
+    gu = (torch.randn(R, 2 * I, generator=gen, device=cuda_dev) * 3).to(torch.bfloat16)
+    dh = torch.randn(R, I, generator=gen, device=cuda_dev).to(torch.bfloat16)
+    dgu = mxg.ops.swiglu_bwd(gu, dh)
+    ref_in = gu.float().requires_grad_(True)
+    out = torch.nn.functional.silu(ref_in[:, :I]) * ref_in[:, I:]
+    out.backward(dh.float())
+    ref = ref_in.grad
+    err = ((dgu.float() - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+    assert err <= 1e-2
