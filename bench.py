@@ -103,8 +103,16 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
+        self.reader = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
@@ -112,18 +120,26 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        t0 = time.time()  # the timed region starts once sampling runs (first sample)
+        while not self.lines and time.time() - t0 < 10 and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.lines.clear()
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
+            time.sleep(0.25)   # let the sample covering the end of the region arrive
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self.proc.wait()
+            if self.reader is not None:
+                self.reader.join(timeout=5)
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()

@@ -328,7 +328,8 @@ struct GemmArgs {
   int* err;
   uint64_t timeout_ns;
   int stall_test;
-  int fwd_tma_store;  // forward output row stride is 16-byte aligned: store via TMA
+  int fwd_tma_store;    // forward output row stride is 16-byte aligned: store via TMA
+  int wgrad_tma_store;  // wgrad output row stride is 16-byte aligned: store via TMA
 };
 
 struct __align__(1024) SmemLayout {
@@ -336,7 +337,7 @@ struct __align__(1024) SmemLayout {
   uint8_t b[kStages][kBBytes];
   uint8_t sfa[kStages][kSfaBytes];
   uint8_t sfb[kStages][kSfbBytes];
-  alignas(1024) uint8_t epi[4][4096];  // per epilogue warp: 32 rows x 128 B staging, 128-byte swizzle
+  alignas(1024) uint8_t epi[4][4096];  // per epilogue warp: 4 KiB staging (two 2 KiB slots), swizzled
   uint64_t full[kStages];      // leader: both CTAs' loads of the stage landed
   uint64_t empty[kStages];     // each CTA: the pair MMA finished reading the stage
   uint64_t acc_full[2];        // each CTA: accumulator buffer complete
@@ -657,14 +658,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 0-3, both CTAs)
+    // TMEM loads are software-pipelined one 32-column chunk ahead; staged
+    // chunks leave through TMA stores from two 2 KiB slots per warp, so the
+    // next chunk is written while the previous store still reads its slot.
     const int row = warp * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
+    uint32_t slot = 0;         // staging slot (2 KiB half of s.epi[warp]) the next store uses
     bool epi_pending = false;  // a TMA store of this warp may still read its staging buffer
+    uint8_t* const epi = s.epi[warp];
+    const bool f32 = g.out_dtype == MXG_DTYPE_F32;
+    // free the slot about to be written: at most the other slot's store may still read
+    auto slot_ready = [&]() {
+      if (epi_pending) {
+        if (lane == 0) bulk_wait_group_read1();
+        __syncwarp();
+      }
+    };
+    auto issue_store = [&](const CUtensorMap* tm, uint32_t src, int x, int y, int z, bool three_d) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (three_d) tma_store_3d(tm, src, x, y, z);
+        else tma_store_2d(tm, src, x, y);
+        bulk_commit_group();
+      }
+      epi_pending = true;
+    };
     for (int t = pair; t < num_tiles; t += npairs) {
       const TileInfo ti = decode_tile<MODE>(s, g, t, rank);
-      uint32_t v[32];
       if (ti.kb_count == 0) {  // empty group (wgrad): dW[e] = 0
-        for (int c0 = 0; c0 < ti.nlen; c0 += 32) store_chunk<MODE>(g, ti, row, c0, v, true);
+        uint32_t z[32];
+        for (int c0 = 0; c0 < ti.nlen; c0 += 32) store_chunk<MODE>(g, ti, row, c0, z, true);
         continue;
       }
       bool ok = mbar_wait(smem_u32(&s.acc_full[acc]), acc_phase, wc);
@@ -672,67 +696,89 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (uint32_t(warp * 32) << 16) + acc * kAccStride;
-      const bool tma_out = MODE == MODE_WGRAD && g.out_dtype == MXG_DTYPE_F32;
-      const bool f32 = g.out_dtype == MXG_DTYPE_F32;
-      for (int c0 = 0; c0 < ti.nlen; c0 += 32) {
-        tmem_ld_32x32b_x32(tb + uint32_t(c0), v);
-        tmem_ld_wait();
-        if (c0 + 32 >= ti.nlen) {  // accumulator fully read: let the next tile's MMAs start
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&s.acc_empty[acc]), 0));
-        }
-        const int rows_here = min(32, ti.nlen - c0);
-        if (MODE == MODE_FWD && g.fwd_tma_store && (rows_here == 32 || rows_here == 16)) {
-          // forward: this warp holds 32 features (lanes) x 32 tokens (columns);
-          // stage it transposed as [token][feature] and store whole token rows
-          uint8_t* buf = s.epi[warp];
-          if (epi_pending) {  // the previous store has finished reading the buffer
-            if (lane == 0) bulk_wait_group_read0();
-            __syncwarp();
-          }
-          if (f32) {  // 128-byte rows, 128-byte swizzle
+      const uint32_t acc_empty_leader = mapa_shared(smem_u32(&s.acc_empty[acc]), 0);
+      auto release_acc = [&]() {  // accumulator fully read: let the next tile's MMAs start
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+      };
+      auto emit = [&](int c0, const uint32_t (&v)[32]) {
+        const int cols_here = min(32, ti.nlen - c0);
+        if (MODE == MODE_FWD && g.fwd_tma_store && (cols_here == 32 || cols_here == 16)) {
+          // this warp holds 32 features (lanes) x 32 tokens (columns): stage it
+          // transposed as [token][feature] and store whole token rows
+          const int f0 = ti.mb * kBM + warp * 32;
+          if (f32) {  // 32 tokens x 128 B, 128-byte swizzle: the whole 4 KiB buffer
+            if (epi_pending) {
+              if (lane == 0) bulk_wait_group_read0();
+              __syncwarp();
+            }
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              *reinterpret_cast<uint32_t*>(buf + j * 128 + (((lane >> 2) ^ (j & 7)) * 16) +
+              *reinterpret_cast<uint32_t*>(epi + j * 128 + (((lane >> 2) ^ (j & 7)) * 16) +
                                            (lane & 3) * 4) = v[j];
-          } else {    // 64-byte rows, 64-byte swizzle
+            issue_store(cols_here == 32 ? &tmOut : &tmOut16, smem_u32(epi), f0, ti.b_row + c0, 0, false);
+            slot = 0;
+          } else {    // 32 tokens x 64 B, 64-byte swizzle: one 2 KiB slot
+            slot_ready();
+            uint8_t* buf = epi + slot * 2048;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               *reinterpret_cast<__nv_bfloat16*>(buf + j * 64 + (((lane >> 3) ^ ((j >> 1) & 3)) * 16) +
                                                 (lane & 7) * 2) =
                   __float2bfloat16_rn(__uint_as_float(v[j]));
+            issue_store(cols_here == 32 ? &tmOut : &tmOut16, smem_u32(buf), f0, ti.b_row + c0, 0, false);
+            slot ^= 1u;
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            const int f0 = ti.mb * kBM + warp * 32;
-            if (rows_here == 32) tma_store_2d(&tmOut, smem_u32(buf), f0, ti.b_row + c0);
-            else tma_store_2d(&tmOut16, smem_u32(buf), f0, ti.b_row + c0);
-            bulk_commit_group();
-          }
-          epi_pending = true;
-        } else if (tma_out && c0 + 32 <= ti.nlen) {
-          // stage this warp's 32 x 32 fp32 block (row = lane) in the 128-byte
-          // swizzled layout the store's tensor map expects, then one TMA store
-          uint8_t* buf = s.epi[warp];
-          if (epi_pending) {
-            if (lane == 0) bulk_wait_group_read0();
-            __syncwarp();
-          }
+        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && f32) {
+          // row = lane, 16 fp32 columns (64 B) per store, 64-byte swizzle; the
+          // store clips at the tensor edge, and a half past this tile's
+          // columns is skipped
+          const int r0 = ti.mb * kBM + warp * 32;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) * 16)) =
-                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_3d(&tmOut, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e);
-            bulk_commit_group();
+          for (int h = 0; h < 2; ++h) {
+            if (c0 + 16 * h < ti.nlen) {
+              slot_ready();
+              uint8_t* buf = epi + slot * 2048;
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                *reinterpret_cast<uint4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) =
+                    make_uint4(v[16 * h + 4 * u], v[16 * h + 4 * u + 1], v[16 * h + 4 * u + 2],
+                               v[16 * h + 4 * u + 3]);
+              issue_store(&tmOut, smem_u32(buf), ti.n0 + c0 + 16 * h, r0, ti.e, true);
+              slot ^= 1u;
+            }
           }
-          epi_pending = true;
+        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && cols_here == 32) {
+          // bf16: row = lane, 32 columns (64 B), 64-byte swizzle
+          slot_ready();
+          uint8_t* buf = epi + slot * 2048;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) = make_uint4(
+                pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
+          issue_store(&tmOut, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e, true);
+          slot ^= 1u;
         } else {
           store_chunk<MODE>(g, ti, row, c0, v, false);
+        }
+      };
+      const int nchunks = (ti.nlen + 31) >> 5;
+      uint32_t va[32], vb[32];
+      tmem_ld_32x32b_x32(tb, va);
+      for (int ci = 0; ci < nchunks; ci += 2) {
+        tmem_ld_wait_regs(va);
+        if (ci + 1 < nchunks) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 1)), vb);
+        else release_acc();
+        emit(32 * ci, va);
+        if (ci + 1 < nchunks) {
+          tmem_ld_wait_regs(vb);
+          if (ci + 2 < nchunks) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 2)), va);
+          else release_acc();
+          emit(32 * (ci + 1), vb);
         }
       }
       acc ^= 1u;
@@ -818,17 +864,22 @@ static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, 
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
-// dW [E, rows, cols] fp32 output, box {32 cols, 32 rows, 1}, 128-byte swizzle.
-static int make_out_tmap_f32(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols) {
+// dW [E, rows, cols] output, box {64 bytes of columns (16 fp32 or 32 bf16),
+// 32 rows, 1}, 64-byte swizzle (the epilogue's staging layout).
+static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols,
+                               int out_dtype) {
   auto enc = get_encode_fn();
   if (!enc) return MXG_ERR_CUDA;
+  const bool f32 = out_dtype == MXG_DTYPE_F32;
+  const cuuint64_t esz = f32 ? 4 : 2;
   cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(E)};
-  cuuint64_t strides[2] = {cuuint64_t(cols) * 4, cuuint64_t(cols) * 4 * cuuint64_t(rows)};
-  cuuint32_t box[3] = {32, 32, 1};
+  cuuint64_t strides[2] = {cuuint64_t(cols) * esz, cuuint64_t(cols) * esz * cuuint64_t(rows)};
+  cuuint32_t box[3] = {cuuint32_t(64 / esz), 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                   base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
@@ -973,8 +1024,11 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   st = make_sf_tmap(&tmSFB, wsb + L.sfb_off, std::max<int64_t>(2 * L.sfb_chunks, 2), 2);
   if (st) return st;
   CUtensorMap tmOut = tmA, tmOut16 = tmA;  // epilogue store maps (unused ones stay dummies)
-  if (P.mode == MODE_WGRAD && out_dtype == MXG_DTYPE_F32) {
-    st = make_out_tmap_f32(&tmOut, out, P.E, P.n_out, P.n_ext);
+  const int64_t out_esz = out_dtype == MXG_DTYPE_F32 ? 4 : 2;
+  // TMA stores need the output row stride to be a multiple of 16 bytes
+  const bool wgrad_tma = P.mode == MODE_WGRAD && (P.n_ext * out_esz) % 16 == 0;
+  if (wgrad_tma) {
+    st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype);
     if (st) return st;
   }
   // TMA stores need the output row stride (N elements) to be a multiple of 16 bytes
@@ -999,6 +1053,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
   ga.stall_test = stall > 0 ? 1 : 0;
   ga.fwd_tma_store = fwd_tma ? 1 : 0;
+  ga.wgrad_tma_store = wgrad_tma ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

@@ -192,6 +192,9 @@ def test_cfg0_wgrad_fixture(mxg, orc, cuda_dev):
     ([512], 128, 496),
     ([0, 64], 384, 16),
     ([1024, 32, 32], 256, 2048),
+    ([64, 32], 128, 112),        # one column tile ending in a 16-column half chunk
+    ([96, 32], 160, 48),
+    ([256, 0, 2048], 300, 7168),  # many column tiles, rows past the last 128-row block
 ])
 def test_wgrad_ragged(mxg, orc, cuda_dev, sizes, N, K):
     gen = torch.Generator(device=cuda_dev).manual_seed(sum(sizes) + N + K)
