@@ -391,10 +391,10 @@ def sample_experts(wl, n=2):
 
 # ---------------------------------------------------------------- EP layer (config 5)
 EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
-# our kernels per layer step: route 3, dispatch gathers 2+1, dy dispatch 2, row
-# quantisations 3, grouped fwd 3 x 5, swiglu 1 + bwd 1, col quantisations 4,
+# our kernels per layer step: route 3, dispatch gathers 2+1, dy dispatch 2,
+# fused quantisations 4 (x, swiglu, dy, swiglu backward), grouped fwd 3 x 5,
 # wgrad 2 x 4, combine gather + combine 2
-EP_LAUNCHES_PER_STEP = 3 + 3 + 2 + 3 + 15 + 2 + 4 + 8 + 2
+EP_LAUNCHES_PER_STEP = 3 + 3 + 2 + 4 + 15 + 8 + 2
 
 
 class EpLayerBench:

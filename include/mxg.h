@@ -165,6 +165,25 @@ MXG_API int mxg_grouped_wgrad_run(const void* go, const void* ia, int num_groups
                                   int64_t n, int64_t k, void* out, int out_dtype, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* Both MXFP8 encodings of x [rows, cols] bf16 in one pass: row-wise (q, s as
+ * mxg_quantize_rowwise) and column-wise (qt, st as mxg_quantize_colwise),
+ * bit-identical to those two.  rows and cols multiples of 32; either output
+ * pair may be null (not both). */
+MXG_API int mxg_quantize_dual(const void* x_bf16, int64_t rows, int64_t cols, void* q_e4m3,
+                              void* scales_e8m0, void* qt_e4m3, void* scales_t_e8m0, void* stream);
+
+/* MXFP8 encodings of h = silu(g) * u for gu rows [g (inter) | u (inter)]
+ * (bf16 [rows, 2*inter]) without writing h: bit-identical to mxg_swiglu
+ * followed by mxg_quantize_dual on its output.  rows, inter multiples of 32. */
+MXG_API int mxg_swiglu_quantize(const void* gu_bf16, int64_t rows, int64_t inter, void* q_e4m3,
+                                void* scales_e8m0, void* qt_e4m3, void* scales_t_e8m0, void* stream);
+
+/* MXFP8 encodings of dgu = mxg_swiglu_bwd(gu, dh) ([rows, 2*inter]) without
+ * writing dgu; bit-identical to the unfused pair. */
+MXG_API int mxg_swiglu_bwd_quantize(const void* gu_bf16, const void* dh_bf16, int64_t rows,
+                                    int64_t inter, void* q_e4m3, void* scales_e8m0, void* qt_e4m3,
+                                    void* scales_t_e8m0, void* stream);
+
 /* ---- expert parallelism: token routing (experts sharded evenly over ranks) ----
  * Global expert e lives on rank e / E_local as local expert e % E_local.  The
  * reference relies on torchtitan's MoE token dispatcher for this step

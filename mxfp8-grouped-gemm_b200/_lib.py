@@ -58,6 +58,9 @@ _PROTOS = {
     "mxg_ep_combine": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_i64, _vp, _vp]),
     "mxg_swiglu": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
     "mxg_swiglu_bwd": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp]),
+    "mxg_quantize_dual": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
+    "mxg_swiglu_quantize": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
+    "mxg_swiglu_bwd_quantize": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_debug_inject_stall": (_c_int, [_c_i64]),
 }
 

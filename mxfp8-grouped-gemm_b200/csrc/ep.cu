@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "mxg.h"
+#include "mxg_device.cuh"
 #include "mxg_internal.h"
 
 namespace mxg {
@@ -236,9 +237,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
     for (int q = 0; q < 4; ++q) {
       const float2 g = __bfloat1622float2(g2[q]);
       const float2 u = __bfloat1622float2(u2[q]);
-      const float a = g.x / (1.0f + __expf(-g.x)) * u.x;
-      const float b = g.y / (1.0f + __expf(-g.y)) * u.y;
-      o2[q] = __floats2bfloat162_rn(a, b);
+      o2[q] = __floats2bfloat162_rn(silu_mul(g.x, u.x), silu_mul(g.y, u.y));
     }
     *reinterpret_cast<uint4*>(h + r * inter + c) = o;
   }
@@ -269,10 +268,11 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const __nv_bfloat16* __
       const float2 g = __bfloat1622float2(g2[q]);
       const float2 u = __bfloat1622float2(u2[q]);
       const float2 d = __bfloat1622float2(d2[q]);
-      const float sx = 1.0f / (1.0f + __expf(-g.x)), sy = 1.0f / (1.0f + __expf(-g.y));
-      og2[q] = __floats2bfloat162_rn(d.x * u.x * sx * (1.0f + g.x * (1.0f - sx)),
-                                     d.y * u.y * sy * (1.0f + g.y * (1.0f - sy)));
-      ou2[q] = __floats2bfloat162_rn(d.x * g.x * sx, d.y * g.y * sy);
+      float dgx, dux, dgy, duy;
+      silu_mul_grad(g.x, u.x, d.x, dgx, dux);
+      silu_mul_grad(g.y, u.y, d.y, dgy, duy);
+      og2[q] = __floats2bfloat162_rn(dgx, dgy);
+      ou2[q] = __floats2bfloat162_rn(dux, duy);
     }
     *reinterpret_cast<uint4*>(dgu + r * 2 * inter + c) = og;
     *reinterpret_cast<uint4*>(dgu + r * 2 * inter + inter + c) = ou;

@@ -13,49 +13,10 @@
 #include <cuda_runtime.h>
 
 #include "mxg.h"
+#include "mxg_device.cuh"
 #include "mxg_internal.h"
 
 namespace mxg {
-
-__device__ __forceinline__ uint32_t rceil_byte(uint32_t amax_bits16) {
-  if (amax_bits16 == 0) return 0u;
-  if (amax_bits16 > 0x7F80u) return 255u;
-  if (amax_bits16 == 0x7F80u) return 254u;
-  const uint32_t f = amax_bits16 << 16;
-  const int e = int(f >> 23) - 127 - 8 + ((f & 0x7FFFFFu) > 0x600000u ? 1 : 0);
-  const int c = e < -127 ? -127 : (e > 127 ? 127 : e);
-  return uint32_t(c + 127);
-}
-
-// Multiplier applied before the e4m3 cast: 1.0 for byte 0, else 2^(127-byte)
-// built directly as an fp32 bit pattern (subnormal for bytes 254 and 255).
-__device__ __forceinline__ float descale_of(uint32_t b) {
-  if (b == 0u) return 1.0f;
-  if (b <= 253u) return __uint_as_float((254u - b) << 23);
-  return __uint_as_float(b == 254u ? 0x00400000u : 0x00200000u);
-}
-
-// Two fp32 values -> two e4m3 codes (low byte = first value), round to
-// nearest even with saturation to +-448.
-__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
-  __nv_fp8x2_storage_t s = __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
-  return uint32_t(s);
-}
-
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-
-__device__ __forceinline__ uint32_t amax2(uint32_t w) {
-  const uint32_t a = w & 0x7FFFu, b = (w >> 16) & 0x7FFFu;
-  return a > b ? a : b;
-}
-
-// NaN-carrying block (scale byte 0xFF): patch the NaN lanes so their codes
-// keep the input's sign, as torch's float8_e4m3fn cast does.
-__device__ __forceinline__ uint32_t fix_nan_byte(uint32_t code, uint32_t bf16bits) {
-  if ((bf16bits & 0x7FFFu) > 0x7F80u) return 0x7Fu | ((bf16bits >> 8) & 0x80u);
-  return code;
-}
 
 // ---------------------------------------------------------------- row-wise
 // One thread per 16-byte chunk (8 bf16); four consecutive lanes form one
@@ -185,6 +146,193 @@ __global__ void __launch_bounds__(kColThreads) quant_colwise_kernel(
   }
 }
 
+// ---------------------------------------------------------------- fused: both directions
+// One pass over a bf16 tensor [rows, cols] (rows a multiple of 32) producing
+// the row-wise (1x32) and/or the column-wise (32x1, transposed) encodings,
+// each bit-identical to the dedicated kernels above.  A block owns a tile of
+// 32 rows x 256 columns: every thread takes four 16-byte chunks (a warp reads
+// one 512-byte row segment), encodes them row-wise in registers (four lanes
+// per 32-element block, as the row-wise kernel), parks them in shared memory,
+// and after a barrier each thread encodes one tile column (32 rows) for the
+// transposed output.  The tensor may be computed on the fly from its inputs
+// (SwiGLU, and the SwiGLU gradient), rounded to bf16 exactly as the unfused
+// kernels round their outputs, so it is never written to memory.
+enum { DUAL_PLAIN = 0, DUAL_SWIGLU = 1, DUAL_SWIGLU_GRAD = 2 };
+constexpr int kTileCols = 256;
+
+struct DualArgs {
+  const uint4* a;    // x (plain) or gu (swiglu variants), rows of 16-byte chunks
+  const uint4* dh;   // swiglu gradient: dh [rows, inter]
+  int64_t rows;
+  int64_t cols;      // columns of the encoded tensor
+  int64_t inter;     // swiglu variants: I
+  uint8_t* q;        // row-wise codes [rows, cols] (null: skip)
+  uint8_t* s;        // row-wise scales [rows, cols/32]
+  uint8_t* qt;       // column-wise codes [cols, rows] (null: skip)
+  uint8_t* st;       // column-wise scales [cols, rows/32]
+};
+
+__device__ __forceinline__ uint4 swiglu_chunk(uint4 g, uint4 u) {
+  return make_uint4(pack2_bf16(silu_mul(bf16_lo(g.x), bf16_lo(u.x)), silu_mul(bf16_hi(g.x), bf16_hi(u.x))),
+                    pack2_bf16(silu_mul(bf16_lo(g.y), bf16_lo(u.y)), silu_mul(bf16_hi(g.y), bf16_hi(u.y))),
+                    pack2_bf16(silu_mul(bf16_lo(g.z), bf16_lo(u.z)), silu_mul(bf16_hi(g.z), bf16_hi(u.z))),
+                    pack2_bf16(silu_mul(bf16_lo(g.w), bf16_lo(u.w)), silu_mul(bf16_hi(g.w), bf16_hi(u.w))));
+}
+
+__device__ __forceinline__ void swiglu_grad_word(uint32_t g, uint32_t u, uint32_t d, uint32_t& dg,
+                                                 uint32_t& du) {
+  float dg0, du0, dg1, du1;
+  silu_mul_grad(bf16_lo(g), bf16_lo(u), bf16_lo(d), dg0, du0);
+  silu_mul_grad(bf16_hi(g), bf16_hi(u), bf16_hi(d), dg1, du1);
+  dg = pack2_bf16(dg0, dg1);
+  du = pack2_bf16(du0, du1);
+}
+
+// Row-wise encoding of one 8-element chunk; the four lanes of its 32-element
+// block must call this together.
+__device__ __forceinline__ void encode_row_chunk(const DualArgs& a, uint4 v, int64_t row,
+                                                 int64_t col, bool valid) {
+  uint32_t m = max(max(amax2(v.x), amax2(v.y)), max(amax2(v.z), amax2(v.w)));
+  m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  const uint32_t b = rceil_byte(m);
+  const float f = descale_of(b);
+  uint32_t c0 = cvt_e4m3x2(bf16_lo(v.x) * f, bf16_hi(v.x) * f);
+  uint32_t c1 = cvt_e4m3x2(bf16_lo(v.y) * f, bf16_hi(v.y) * f);
+  uint32_t c2 = cvt_e4m3x2(bf16_lo(v.z) * f, bf16_hi(v.z) * f);
+  uint32_t c3 = cvt_e4m3x2(bf16_lo(v.w) * f, bf16_hi(v.w) * f);
+  uint32_t lo = c0 | (c1 << 16), hi = c2 | (c3 << 16);
+  if (b == 255u) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t bytes[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t word = j < 2 ? lo : hi;
+      const int sh = (j & 1) * 16;
+      bytes[2 * j] = fix_nan_byte((word >> sh) & 0xFFu, w[j] & 0xFFFFu);
+      bytes[2 * j + 1] = fix_nan_byte((word >> (sh + 8)) & 0xFFu, w[j] >> 16);
+    }
+    lo = bytes[0] | (bytes[1] << 8) | (bytes[2] << 16) | (bytes[3] << 24);
+    hi = bytes[4] | (bytes[5] << 8) | (bytes[6] << 16) | (bytes[7] << 24);
+  }
+  if (valid) {
+    __stcs(reinterpret_cast<uint2*>(a.q + row * a.cols + col), make_uint2(lo, hi));
+    if ((threadIdx.x & 3) == 0) a.s[row * (a.cols / 32) + col / 32] = uint8_t(b);
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) quant_dual_kernel(DualArgs a) {
+  __shared__ __align__(16) uint16_t tile[32][kTileCols];
+  const int64_t r0 = int64_t(blockIdx.y) * 32;
+  const int t = threadIdx.x;
+  // tile columns -> tensor columns: contiguous, except for the gradient where
+  // tile columns [0,128) are dg[j0 + c] and [128,256) are du[j0 + c - 128]
+  const int64_t c0 = KIND == DUAL_SWIGLU_GRAD ? int64_t(blockIdx.x) * (kTileCols / 2)
+                                              : int64_t(blockIdx.x) * kTileCols;
+  if (KIND != DUAL_SWIGLU_GRAD) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = t + 256 * i;          // chunk of the tile: row k / 32, chunk k % 32
+      const int r = k >> 5, ch = k & 31;
+      const int64_t col = c0 + ch * 8;
+      const bool valid = col < a.cols;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        if (KIND == DUAL_PLAIN) {
+          v = __ldcs(a.a + ((r0 + r) * a.cols + col) / 8);
+        } else {
+          const uint4* rowp = a.a + (r0 + r) * (2 * a.inter) / 8;
+          v = swiglu_chunk(__ldcs(rowp + col / 8), __ldcs(rowp + (a.inter + col) / 8));
+        }
+      }
+      if (a.q) encode_row_chunk(a, v, r0 + r, col, valid);
+      *reinterpret_cast<uint4*>(&tile[r][ch * 8]) = v;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int k = t + 256 * i;          // input chunk: row k / 16, j-chunk k % 16
+      const int r = k >> 4, ch = k & 15;
+      const int64_t j = c0 + ch * 8;
+      const bool valid = j < a.inter;
+      uint4 dg = make_uint4(0, 0, 0, 0), du = dg;
+      if (valid) {
+        const uint4* rowp = a.a + (r0 + r) * (2 * a.inter) / 8;
+        const uint4 g = __ldcs(rowp + j / 8), u = __ldcs(rowp + (a.inter + j) / 8);
+        const uint4 d = __ldcs(a.dh + ((r0 + r) * a.inter + j) / 8);
+        swiglu_grad_word(g.x, u.x, d.x, dg.x, du.x);
+        swiglu_grad_word(g.y, u.y, d.y, dg.y, du.y);
+        swiglu_grad_word(g.z, u.z, d.z, dg.z, du.z);
+        swiglu_grad_word(g.w, u.w, d.w, dg.w, du.w);
+      }
+      if (a.q) {
+        encode_row_chunk(a, dg, r0 + r, j, valid);
+        encode_row_chunk(a, du, r0 + r, a.inter + j, valid);
+      }
+      *reinterpret_cast<uint4*>(&tile[r][ch * 8]) = dg;
+      *reinterpret_cast<uint4*>(&tile[r][128 + ch * 8]) = du;
+    }
+  }
+  if (a.qt == nullptr) return;
+  __syncthreads();
+  // column pass: thread t encodes tile column t over the 32 rows
+  int64_t col;
+  if (KIND == DUAL_SWIGLU_GRAD) {
+    const int64_t j = c0 + (t & 127);
+    if (j >= a.inter) return;
+    col = t < 128 ? j : a.inter + j;
+  } else {
+    col = c0 + t;
+    if (col >= a.cols) return;
+  }
+  uint32_t w[16];  // rows 2i (low half) and 2i+1 (high half)
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    w[i] = uint32_t(tile[2 * i][t]) | (uint32_t(tile[2 * i + 1][t]) << 16);
+    m = max(m, amax2(w[i]));
+  }
+  const uint32_t b = rceil_byte(m);
+  const float f = descale_of(b);
+  uint32_t out[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint32_t lo = cvt_e4m3x2(bf16_lo(w[2 * j]) * f, bf16_hi(w[2 * j]) * f);
+    uint32_t hi = cvt_e4m3x2(bf16_lo(w[2 * j + 1]) * f, bf16_hi(w[2 * j + 1]) * f);
+    if (b == 255u) {
+      lo = fix_nan_byte(lo & 0xFFu, w[2 * j] & 0xFFFFu) |
+           (fix_nan_byte((lo >> 8) & 0xFFu, w[2 * j] >> 16) << 8);
+      hi = fix_nan_byte(hi & 0xFFu, w[2 * j + 1] & 0xFFFFu) |
+           (fix_nan_byte((hi >> 8) & 0xFFu, w[2 * j + 1] >> 16) << 8);
+    }
+    out[j] = lo | (hi << 16);
+  }
+  uint4* d = reinterpret_cast<uint4*>(a.qt + col * a.rows + r0);
+  __stcs(d, make_uint4(out[0], out[1], out[2], out[3]));
+  __stcs(d + 1, make_uint4(out[4], out[5], out[6], out[7]));
+  a.st[col * (a.rows / 32) + blockIdx.y] = uint8_t(b);
+}
+
+template <int KIND>
+static int launch_dual(DualArgs a, void* stream) {
+  if (a.rows < 0 || a.cols < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if ((a.q == nullptr) != (a.s == nullptr) || (a.qt == nullptr) != (a.st == nullptr) ||
+      (a.q == nullptr && a.qt == nullptr))
+    return MXG_ERR_INVALID_ARGUMENT;
+  if (a.rows % 32 != 0 || a.cols % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  if ((a.q && !aligned16(a.q)) || (a.qt && !aligned16(a.qt))) return MXG_ERR_MISALIGNED;
+  if (a.rows == 0 || a.cols == 0) return MXG_OK;
+  if (a.rows / 32 > 65535) return MXG_ERR_BAD_SHAPE;
+  int e = check_device();
+  if (e) return e;
+  const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
+  const int64_t per = KIND == DUAL_SWIGLU_GRAD ? kTileCols / 2 : kTileCols;
+  dim3 grid(unsigned((span + per - 1) / per), unsigned(a.rows / 32));
+  quant_dual_kernel<KIND><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
 // ---------------------------------------------------------------- transpose
 // dst [cols, rows] = src [rows, cols]^T for bytes, 64x64 tiles through smem.
 __global__ void __launch_bounds__(256) transpose_u8_kernel(const uint8_t* __restrict__ src,
@@ -255,4 +403,38 @@ extern "C" int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, voi
   transpose_u8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const uint8_t*>(src), rows, cols, reinterpret_cast<uint8_t*>(dst));
   return cuda_status(cudaGetLastError());
+}
+
+extern "C" int mxg_quantize_dual(const void* x_bf16, int64_t rows, int64_t cols, void* q_e4m3,
+                                 void* scales_e8m0, void* qt_e4m3, void* scales_t_e8m0,
+                                 void* stream) {
+  if (!x_bf16) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x_bf16)) return MXG_ERR_MISALIGNED;
+  DualArgs a{reinterpret_cast<const uint4*>(x_bf16), nullptr, rows, cols, 0,
+             reinterpret_cast<uint8_t*>(q_e4m3), reinterpret_cast<uint8_t*>(scales_e8m0),
+             reinterpret_cast<uint8_t*>(qt_e4m3), reinterpret_cast<uint8_t*>(scales_t_e8m0)};
+  return launch_dual<DUAL_PLAIN>(a, stream);
+}
+
+extern "C" int mxg_swiglu_quantize(const void* gu_bf16, int64_t rows, int64_t inter, void* q_e4m3,
+                                   void* scales_e8m0, void* qt_e4m3, void* scales_t_e8m0,
+                                   void* stream) {
+  if (!gu_bf16) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gu_bf16)) return MXG_ERR_MISALIGNED;
+  DualArgs a{reinterpret_cast<const uint4*>(gu_bf16), nullptr, rows, inter, inter,
+             reinterpret_cast<uint8_t*>(q_e4m3), reinterpret_cast<uint8_t*>(scales_e8m0),
+             reinterpret_cast<uint8_t*>(qt_e4m3), reinterpret_cast<uint8_t*>(scales_t_e8m0)};
+  return launch_dual<DUAL_SWIGLU>(a, stream);
+}
+
+extern "C" int mxg_swiglu_bwd_quantize(const void* gu_bf16, const void* dh_bf16, int64_t rows,
+                                       int64_t inter, void* q_e4m3, void* scales_e8m0,
+                                       void* qt_e4m3, void* scales_t_e8m0, void* stream) {
+  if (!gu_bf16 || !dh_bf16) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gu_bf16) || !aligned16(dh_bf16)) return MXG_ERR_MISALIGNED;
+  DualArgs a{reinterpret_cast<const uint4*>(gu_bf16), reinterpret_cast<const uint4*>(dh_bf16),
+             rows, 2 * inter, inter, reinterpret_cast<uint8_t*>(q_e4m3),
+             reinterpret_cast<uint8_t*>(scales_e8m0), reinterpret_cast<uint8_t*>(qt_e4m3),
+             reinterpret_cast<uint8_t*>(scales_t_e8m0)};
+  return launch_dual<DUAL_SWIGLU_GRAD>(a, stream);
 }

@@ -5,11 +5,13 @@ projection, SiLU-gated product, down projection per expert, under torchtitan's
 token dispatcher with MXFP8 grouped GEMMs patched in, ``port_mxfp8.py:175-194``)
 built from this library's pieces:
 
-forward   dispatch x -> quantize 1x32 -> gate/up grouped fwd -> swiglu ->
-          quantize -> down grouped fwd -> combine (weighted by router probs)
-backward  dispatch dy along the same plan -> quantize -> down dgrad (grouped
-          fwd against the pre-quantised transposed down weights) -> swiglu
-          backward -> 32x1 quantisations -> down and gate/up weight gradients
+forward   dispatch x -> quantize (1x32 and 32x1 in one pass) -> gate/up
+          grouped fwd -> swiglu fused with its quantisation -> down grouped
+          fwd -> combine (weighted by router probs)
+backward  dispatch dy along the same plan -> quantize (both directions) ->
+          down dgrad (grouped fwd against the pre-quantised transposed down
+          weights) -> down wgrad -> swiglu backward fused with its 32x1
+          quantisation -> gate/up wgrad
 
 Weights are quantised once (static between optimiser steps).  With a comm
 stream the dy dispatch runs under the forward GEMMs and the combine under the
@@ -84,32 +86,28 @@ class ExpertFFN:
             dy_local = ep.dispatch_like(dy, plan)
             dy_ready = torch.cuda.Event()
             dy_ready.record()
-        xq = ops.quantize_rowwise(x_local)
+        xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
         self._mark("quantize_x")
-        gu = self._fwd(xq, self.wgu, offs)
+        gu = self._fwd((xq, xs), self.wgu, offs)
         self._mark("fwd_gate_up")
-        h = ops.swiglu(gu)
-        hq = ops.quantize_rowwise(h)
+        hq, hs, ia_d, ias_d = ops.swiglu_quantize(gu)        # h is never written in bf16
         self._mark("swiglu_quantize_h")
-        y_local = self._fwd(hq, self.wd, offs)
+        y_local = self._fwd((hq, hs), self.wd, offs)
         self._mark("fwd_down")
         if comm is not None:
             comm.wait_stream(main)
         with side():
             out = ep.combine(y_local, plan, probs)
         main.wait_event(dy_ready)
-        dyq = ops.quantize_rowwise(dy_local)
+        dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
         self._mark("quantize_dy")
-        dh = self._fwd(dyq, self.wdt, offs)
+        dh = self._fwd((dyq, dys), self.wdt, offs)
         self._mark("dgrad_down")
-        dgu = ops.swiglu_bwd(gu, dh)
-        go_d, ia_d = ops.quantize_colwise(dy_local), ops.quantize_colwise(h)
-        self._mark("swiglu_bwd_quantize_down")
-        dw_d = self._wgrad(go_d, ia_d, offs)
+        dw_d = self._wgrad((go_d, gos_d), (ia_d, ias_d), offs)
         self._mark("wgrad_down")
-        go_g, ia_g = ops.quantize_colwise(dgu), ops.quantize_colwise(x_local)
+        _, _, go_g, gos_g = ops.swiglu_bwd_quantize(gu, dh)  # dgu is never written in bf16
         self._mark("quantize_gate_up")
-        dw_gu = self._wgrad(go_g, ia_g, offs)
+        dw_gu = self._wgrad((go_g, gos_g), (ia_g, ias_g), offs)
         self._mark("wgrad_gate_up")
         if comm is not None:
             # Every later use of memory from either stream is ordered after

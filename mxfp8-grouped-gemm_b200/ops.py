@@ -83,6 +83,66 @@ def quantize_colwise(x: torch.Tensor):
     return qt, st
 
 
+def _dual_outputs(R, C, device, rowwise, colwise):
+    q = s = qt = st = None
+    if rowwise:
+        q = torch.empty(R, C, dtype=torch.float8_e4m3fn, device=device)
+        s = torch.empty(R, C // 32, dtype=torch.uint8, device=device)
+    if colwise:
+        qt = torch.empty(C, R, dtype=torch.float8_e4m3fn, device=device)
+        st = torch.empty(C, R // 32, dtype=torch.uint8, device=device)
+    return q, s, qt, st
+
+
+def quantize_dual(x: torch.Tensor, *, rowwise=True, colwise=True):
+    """Both MXFP8 encodings of bf16 x [R, C] in one pass (R, C multiples of
+    32): (q [R, C], s [R, C/32], qt [C, R], st [C, R/32]); a direction not
+    asked for comes back as None."""
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("x must be a 2-D bf16 tensor")
+    x = x.contiguous()
+    R, C = x.shape
+    q, s, qt, st = _dual_outputs(R, C, x.device, rowwise, colwise)
+    _lib.check(_lib.load().mxg_quantize_dual(x.data_ptr(), R, C, _lib.ptr(q), _lib.ptr(s),
+                                             _lib.ptr(qt), _lib.ptr(st), _lib.stream_ptr(x.device)),
+               "mxg_quantize_dual")
+    return q, s, qt, st
+
+
+def swiglu_quantize(gu: torch.Tensor, *, rowwise=True, colwise=True):
+    """MXFP8 encodings of h = silu(g) * u for gu = [g | u] ([R, 2I] bf16)
+    without materialising h; same bytes as ``quantize_dual(swiglu(gu))``."""
+    _cuda(gu, "gu")
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2 or gu.shape[1] % 2:
+        raise ValueError("swiglu_quantize takes a [R, 2I] bf16 tensor")
+    gu = gu.contiguous()
+    R, I = gu.shape[0], gu.shape[1] // 2
+    q, s, qt, st = _dual_outputs(R, I, gu.device, rowwise, colwise)
+    _lib.check(_lib.load().mxg_swiglu_quantize(gu.data_ptr(), R, I, _lib.ptr(q), _lib.ptr(s),
+                                               _lib.ptr(qt), _lib.ptr(st),
+                                               _lib.stream_ptr(gu.device)), "mxg_swiglu_quantize")
+    return q, s, qt, st
+
+
+def swiglu_bwd_quantize(gu: torch.Tensor, dh: torch.Tensor, *, rowwise=False, colwise=True):
+    """MXFP8 encodings of the SwiGLU input gradient dgu ([R, 2I]) without
+    materialising it; same bytes as ``quantize_dual(swiglu_bwd(gu, dh))``."""
+    _cuda(gu, "gu")
+    _cuda(dh, "dh")
+    if gu.dtype != torch.bfloat16 or dh.dtype != torch.bfloat16 or gu.dim() != 2 \
+            or dh.shape != (gu.shape[0], gu.shape[1] // 2) or gu.shape[1] % 2:
+        raise ValueError("swiglu_bwd_quantize takes gu [R, 2I] and dh [R, I], both bf16")
+    gu, dh = gu.contiguous(), dh.contiguous()
+    R, I = dh.shape
+    q, s, qt, st = _dual_outputs(R, 2 * I, gu.device, rowwise, colwise)
+    _lib.check(_lib.load().mxg_swiglu_bwd_quantize(gu.data_ptr(), dh.data_ptr(), R, I, _lib.ptr(q),
+                                                   _lib.ptr(s), _lib.ptr(qt), _lib.ptr(st),
+                                                   _lib.stream_ptr(gu.device)),
+               "mxg_swiglu_bwd_quantize")
+    return q, s, qt, st
+
+
 # ---------------------------------------------------------------- GEMMs
 def grouped_fwd(a, w, offs, a_scales=None, w_scales=None, *, out_dtype=torch.bfloat16,
                 offs_kind=_lib.OFFS_AUTO, out=None):

@@ -71,3 +71,62 @@ def test_full_size_rowwise_sampled(mxg, orc, cuda_dev):
     err = (deq - x.float().view(65536, 224, 32)).abs()
     bound = torch.exp2(s.float() - 127).unsqueeze(-1) * 16.0  # half ulp at the top binade (448 -> 32/2)
     assert bool((err <= bound).all())
+
+
+def _special_bf16(shape, gen, dev, scale=1.0):
+    x = (torch.randn(*shape, generator=gen, device=dev) * scale).to(torch.bfloat16)
+    flat = x.view(-1)
+    n = flat.numel()
+    idx = torch.randint(0, n, (max(1, n // 500),), generator=gen, device=dev)
+    specials = torch.tensor([float("nan"), float("inf"), -float("inf"), 0.0, -0.0, 1e-30, 3e38],
+                            device=dev).to(torch.bfloat16)
+    flat[idx] = specials[torch.arange(idx.numel(), device=dev) % specials.numel()]
+    flat[: 32 * 3] = 0  # an all-zero block in each direction
+    return x
+
+
+@pytest.mark.parametrize("shape", [(32, 32), (64, 96), (4096, 7168), (160, 2048)])
+def test_quantize_dual_matches_separate_kernels(mxg, cuda_dev, shape):
+    gen = torch.Generator(device=cuda_dev).manual_seed(shape[0] + shape[1])
+    x = _special_bf16(shape, gen, cuda_dev)
+    q, s, qt, st = mxg.ops.quantize_dual(x)
+    q1, s1 = mxg.quantize_rowwise(x)
+    qt1, st1 = mxg.quantize_colwise(x)
+    assert torch.equal(q.view(torch.uint8), q1.view(torch.uint8)) and torch.equal(s, s1)
+    assert torch.equal(qt.view(torch.uint8), qt1.view(torch.uint8)) and torch.equal(st, st1)
+    q2, s2, n1, n2 = mxg.ops.quantize_dual(x, colwise=False)
+    assert n1 is None and torch.equal(q2.view(torch.uint8), q1.view(torch.uint8))
+    _, _, qt3, st3 = mxg.ops.quantize_dual(x, rowwise=False)
+    assert torch.equal(qt3.view(torch.uint8), qt1.view(torch.uint8)) and torch.equal(st3, st1)
+
+
+def test_quantize_dual_bits_match_oracle(mxg, orc, cuda_dev):
+    gen = torch.Generator(device=cuda_dev).manual_seed(11)
+    x = _special_bf16((96, 160), gen, cuda_dev, scale=50.0)
+    q, s, qt, st = mxg.ops.quantize_dual(x)
+    bits = _bits(x)
+    rq, rs = orc.quantize_rowwise(bits)
+    cq, cs = orc.quantize_colwise(bits)
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(qt.view(torch.uint8).cpu().numpy(), cq) and np.array_equal(st.cpu().numpy(), cs)
+
+
+@pytest.mark.parametrize("R,I", [(32, 32), (128, 2048), (96, 1536)])
+def test_swiglu_quantize_matches_unfused(mxg, cuda_dev, R, I):
+    gen = torch.Generator(device=cuda_dev).manual_seed(R * 7 + I)
+    gu = (torch.randn(R, 2 * I, generator=gen, device=cuda_dev) * 4).to(torch.bfloat16)
+    fused = mxg.ops.swiglu_quantize(gu)
+    ref = mxg.ops.quantize_dual(mxg.ops.swiglu(gu))
+    for a, b in zip(fused, ref):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
+@pytest.mark.parametrize("R,I", [(32, 32), (128, 2048), (64, 1536)])
+def test_swiglu_bwd_quantize_matches_unfused(mxg, cuda_dev, R, I):
+    gen = torch.Generator(device=cuda_dev).manual_seed(R * 5 + I)
+    gu = (torch.randn(R, 2 * I, generator=gen, device=cuda_dev) * 4).to(torch.bfloat16)
+    dh = (torch.randn(R, I, generator=gen, device=cuda_dev) * 1e-2).to(torch.bfloat16)
+    fused = mxg.ops.swiglu_bwd_quantize(gu, dh, rowwise=True, colwise=True)
+    ref = mxg.ops.quantize_dual(mxg.ops.swiglu_bwd(gu, dh))
+    for a, b in zip(fused, ref):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
