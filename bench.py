@@ -401,7 +401,8 @@ class EpLayerBench:
     """One rank's share of the config-5 layer: resident tokens, routing,
     gradients and its local experts."""
 
-    def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS):
+    def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
+                 transport="auto", p2p_blocks=0):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -411,7 +412,8 @@ class EpLayerBench:
         if placement == "balanced" and world > 1:
             slot = m.ep.balanced_placement(W.expected_expert_load(logp, EP_TOPK), world)
         self.placement = placement if world > 1 else "single"
-        self.ep = m.ExpertParallel(EP_EXPERTS, placement=slot)
+        self.ep = m.ExpertParallel(EP_EXPERTS, placement=slot, transport=transport,
+                                   p2p_max_blocks=p2p_blocks)
         g = torch.Generator(device=dev).manual_seed(seed * 1000 + 17 + rank)
         self.x = torch.randn(tokens, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16)
         self.dy = (torch.randn(tokens, HIDDEN, generator=g, device=dev) * 1e-2).to(torch.bfloat16)
@@ -529,13 +531,14 @@ def measure_ep_layer(lb, world, steps, warmup):
                          "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
                          "peak_source": pk["source"], "traffic": None,
                          "flops_per_launch": flops[dom]},
-            "placement": lb.placement, "overlap": lb.comm is not None}
+            "placement": lb.placement, "overlap": lb.comm is not None, "transport": lb.ep.transport}
 
 
 def run_ep_mxg(args, rank, world, local):
     """The N>1 bench line: config 5 across the process group."""
     pkg()._lib.load()
-    lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=not args.no_overlap)
+    lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=not args.no_overlap,
+                      transport=args.transport, p2p_blocks=args.p2p_blocks)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -553,7 +556,8 @@ def run_ep_mxg(args, rank, world, local):
                       "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
                       "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
                       "hidden": HIDDEN, "intermediate": INTER, "placement": r["placement"],
-                      "comm_overlap": r["overlap"], "parallelism": f"ep{world}",
+                      "comm_overlap": r["overlap"], "transport": r["transport"],
+                      "parallelism": f"ep{world}",
                       "l2": "operands > L2 (no flush needed)"},
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
@@ -808,6 +812,9 @@ def main():
                     help="expert placement for the EP layer (N>1)")
     ap.add_argument("--no-overlap", action="store_true", help="EP layer: collectives on the main stream")
     ap.add_argument("--no-ep", action="store_true", help="N=1: skip the one-GPU EP layer measurement")
+    ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="EP layer token exchange: NVLink peer stores or NCCL all_to_all")
+    ap.add_argument("--p2p-blocks", type=int, default=0, help="grid cap of the peer-store kernels (0: default)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

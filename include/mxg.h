@@ -228,6 +228,51 @@ MXG_API int mxg_swiglu(const void* gu, int64_t rows, int64_t inter, void* h, voi
 MXG_API int mxg_swiglu_bwd(const void* gu, const void* dh, int64_t rows, int64_t inter, void* dgu,
                            void* stream);
 
+/* ---- expert parallelism over NVLink peer memory ----
+ * Receive buffers are shared between the ranks of one node with CUDA IPC; a
+ * dispatch writes every routed row straight into its final (expert-major,
+ * padded) row of the owner's buffer, a combine writes results back to the
+ * token's home rank.  The kernels only store; the caller orders the ranks
+ * with a collective before and after each exchange (replaces the all-to-all
+ * of torchtitan's token dispatcher, port_mxfp8.py:74,240). */
+#define MXG_PEER_HANDLE_BYTES 64
+MXG_API int mxg_peer_alloc(size_t bytes, void** dptr, void* handle_out);
+MXG_API int mxg_peer_open(const void* handle, void** dptr);
+MXG_API int mxg_peer_close(void* dptr);
+MXG_API int mxg_peer_free(void* dptr);
+
+/* From the all-gathered slot counts counts_all [world][num_slots] (slot s on
+ * rank s / (num_slots / world)): this rank's send-position prefix
+ * slot_start [num_slots + 1], dest_base [num_slots] (destination row of send
+ * position p in slot s = dest_base[s] + p), its own padded groups
+ * group_rows / group_start [e_local (+1)], and for each of its m_pad padded
+ * rows the rank and send position the result returns to (back_rank,
+ * back_row; -1 on padding rows). */
+MXG_API size_t mxg_ep_p2p_plan_workspace_size(int world, int num_slots);
+MXG_API int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slots, int me, int pad,
+                            int64_t m_pad, int32_t* slot_start, int32_t* dest_base,
+                            int32_t* group_rows, int32_t* group_start, int32_t* back_rank,
+                            int32_t* back_row, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Row src[send_rows[p]] -> row dest_base[s] + p of peer_bufs[s / e_local]
+ * (peer_bufs: device array of every rank's buffer address).  A destination
+ * row outside [0, capacity_rows) is skipped and sets the device error word.
+ * max_blocks <= 0: the library's default grid. */
+MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
+                                int64_t n_send, const int32_t* slot_start, const int32_t* dest_base,
+                                int num_slots, int e_local, const uint64_t* peer_bufs,
+                                int64_t capacity_rows, int max_blocks, void* stream);
+
+/* Padded local row q -> row back_row[q] of peer_bufs[back_rank[q]] (skipped
+ * where back_rank < 0). */
+MXG_API int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* back_rank,
+                              const int32_t* back_row, int64_t m_pad, const uint64_t* peer_bufs,
+                              int world, int64_t capacity_rows, int max_blocks, void* stream);
+
+/* Zero the rows q < m_pad of buf with back_rank[q] < 0. */
+MXG_API int mxg_ep_zero_pad_rows(void* buf, int64_t row_bytes, const int32_t* back_rank,
+                                 int64_t m_pad, void* stream);
+
 /* ---- byte transpose: dst [cols, rows] = src [rows, cols]^T (uint8) ----------- */
 MXG_API int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, void* dst, void* stream);
 

@@ -17,8 +17,15 @@ LIB_PATH = os.path.join(_HERE, "libmxg.so")
 HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "mxg.h")
 
 MXG_OK = 0
+MXG_ERR_INVALID_ARGUMENT = 1
+MXG_ERR_BAD_SHAPE = 2
+MXG_ERR_MISALIGNED = 3
+MXG_ERR_WORKSPACE_TOO_SMALL = 4
+MXG_ERR_CUDA = 5
 MXG_ERR_DEVICE_TIMEOUT = 6
 MXG_ERR_BAD_OFFSETS = 7
+MXG_ERR_UNSUPPORTED_DEVICE = 8
+MXG_ERR_TOO_MANY_GROUPS = 9
 OFFS_LEADING_ZERO, OFFS_CUMULATIVE, OFFS_SIZES, OFFS_AUTO = 0, 1, 2, 3
 DTYPE_BF16, DTYPE_F32 = 0, 1
 MAX_GROUPS = 256
@@ -58,6 +65,17 @@ _PROTOS = {
     "mxg_ep_combine": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_i64, _vp, _vp]),
     "mxg_swiglu": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
     "mxg_swiglu_bwd": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp]),
+    "mxg_peer_alloc": (_c_int, [_c_size, ctypes.POINTER(_vp), _vp]),
+    "mxg_peer_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "mxg_peer_close": (_c_int, [_vp]),
+    "mxg_peer_free": (_c_int, [_vp]),
+    "mxg_ep_p2p_plan_workspace_size": (_c_size, [_c_int, _c_int]),
+    "mxg_ep_p2p_plan": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _vp, _c_size, _vp]),
+    "mxg_ep_dispatch_p2p": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _vp,
+                                     _c_i64, _c_int, _vp]),
+    "mxg_ep_return_p2p": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _vp, _c_int, _c_i64, _c_int, _vp]),
+    "mxg_ep_zero_pad_rows": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp]),
     "mxg_quantize_dual": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_swiglu_quantize": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_swiglu_bwd_quantize": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),

@@ -1,0 +1,306 @@
+// Expert-parallel dispatch and combine over NVLink peer memory (sm_100a).
+//
+// Every rank exposes receive buffers to the others through CUDA IPC.  A
+// dispatch writes each routed token row straight into its final place in the
+// owner's buffer -- the expert-major, 32-padded layout the grouped GEMMs read
+// -- so there is no send-side gather, no all-to-all staging copy and no
+// receive-side regroup.  The combine writes each result row back into the
+// token's home rank at the row's send position.  These kernels only store
+// (ordinary 16-byte stores to peer addresses); ordering across ranks is left
+// to the caller, who runs a collective before (the count exchange: every
+// receiver is done with the previous contents) and after (every writer is
+// done) each exchange.  No kernel here waits on another rank.
+//
+// Layout of rank d's receive buffer (shared by every rank's plan):
+//   local expert le of rank d occupies padded rows
+//     [gstart_d(le), gstart_d(le) + pad(tot(d, le)))
+//   where tot(d, le) = sum_r C[r][d*E_l + le] and gstart_d is the exclusive
+//   prefix of the padded totals; inside it, the rows sent by rank r come
+//   after those of ranks r' < r, in r's send order.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "mxg.h"
+#include "mxg_internal.h"
+
+namespace mxg {
+
+__host__ __device__ inline int64_t pad_up(int64_t v, int pad) { return (v + pad - 1) / pad * pad; }
+
+// One block.  counts [world][E] (E = world * e_local expert slots).
+// Workspace: pref [world][E + 1] (per-rank exclusive prefix over slots),
+// gs [E] (padded start of every slot in its owner's buffer), tot [E].
+__global__ void p2p_plan_kernel(const int32_t* __restrict__ C, int world, int E, int me, int pad,
+                                int32_t* __restrict__ pref, int32_t* __restrict__ gs,
+                                int32_t* __restrict__ tot, int32_t* __restrict__ slot_start,
+                                int32_t* __restrict__ dest_base, int32_t* __restrict__ group_rows,
+                                int32_t* __restrict__ group_start) {
+  const int e_local = E / world;
+  for (int s = threadIdx.x; s < E; s += blockDim.x) {
+    int32_t t = 0;
+    for (int r = 0; r < world; ++r) t += C[r * E + s];
+    tot[s] = t;
+  }
+  for (int r = threadIdx.x; r < world; r += blockDim.x) {
+    int32_t run = 0;
+    for (int s = 0; s < E; ++s) {
+      pref[r * (E + 1) + s] = run;
+      run += C[r * E + s];
+    }
+    pref[r * (E + 1) + E] = run;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < world; d += blockDim.x) {
+    int32_t run = 0;
+    for (int le = 0; le < e_local; ++le) {
+      gs[d * e_local + le] = run;
+      run += int32_t(pad_up(tot[d * e_local + le], pad));
+    }
+    if (d == me) group_start[e_local] = run;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < E; s += blockDim.x) {
+    int32_t src_off = 0;  // rows of slot s sent by ranks before me
+    for (int r = 0; r < me; ++r) src_off += C[r * E + s];
+    dest_base[s] = gs[s] + src_off - pref[me * (E + 1) + s];
+  }
+  for (int s = threadIdx.x; s <= E; s += blockDim.x) slot_start[s] = pref[me * (E + 1) + s];
+  for (int le = threadIdx.x; le < e_local; le += blockDim.x) {
+    group_rows[le] = int32_t(pad_up(tot[me * e_local + le], pad));
+    group_start[le] = gs[me * e_local + le];
+  }
+}
+
+// One block per local expert of `me`: for every padded row of its group, the
+// rank and send position the result goes back to (-1 on padding rows).
+__global__ void p2p_back_kernel(const int32_t* __restrict__ C, int world, int E, int me, int pad,
+                                const int32_t* __restrict__ pref, const int32_t* __restrict__ gs,
+                                const int32_t* __restrict__ tot, int32_t* __restrict__ back_rank,
+                                int32_t* __restrict__ back_row) {
+  const int e_local = E / world;
+  const int le = blockIdx.x;
+  const int s = me * e_local + le;
+  int32_t q0 = gs[s];
+  for (int r = 0; r < world; ++r) {
+    const int32_t c = C[r * E + s];
+    const int32_t p0 = pref[r * (E + 1) + s];
+    for (int i = threadIdx.x; i < c; i += blockDim.x) {
+      back_rank[q0 + i] = r;
+      back_row[q0 + i] = p0 + i;
+    }
+    q0 += c;
+  }
+  const int32_t end = gs[s] + int32_t(pad_up(tot[s], pad));
+  for (int32_t q = q0 + threadIdx.x; q < end; q += blockDim.x) {
+    back_rank[q] = -1;
+    back_row[q] = -1;
+  }
+}
+
+constexpr int kCopyThreads = 256;
+constexpr int kMaxSlotsSmem = MXG_EP_MAX_EXPERTS + 1;
+
+// Dispatch: send position p (slot s, the largest with slot_start[s] <= p)
+// -> row dest_base[s] + p of rank s / e_local.  One warp per row, 16-byte
+// vectors.
+__global__ void __launch_bounds__(kCopyThreads) p2p_dispatch_kernel(
+    const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ send_rows,
+    int64_t n_send, const int32_t* __restrict__ slot_start, const int32_t* __restrict__ dest_base,
+    int E, int e_local, const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows, int* err) {
+  __shared__ int32_t ss[kMaxSlotsSmem];
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) ss[i] = slot_start[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n_send;
+       p += warps) {
+    int lo = 0, hi = E - 1;  // last slot with ss[s] <= p
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (ss[mid] <= p) lo = mid; else hi = mid - 1;
+    }
+    const int64_t row = int64_t(dest_base[lo]) + p;
+    if (row < 0 || row >= capacity_rows) {
+      if (lane == 0) atomicCAS(err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs;
+    const uint4* s = src + int64_t(send_rows[p]) * row_vecs;
+    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(s + v);
+  }
+  __threadfence_system();
+}
+
+// Combine: padded local row q -> send position back_row[q] of rank back_rank[q].
+__global__ void __launch_bounds__(kCopyThreads) p2p_return_kernel(
+    const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ back_rank,
+    const int32_t* __restrict__ back_row, int64_t m_pad, const uint64_t* __restrict__ peer_bufs,
+    int world, int64_t capacity_rows, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t q = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); q < m_pad;
+       q += warps) {
+    const int r = back_rank[q];
+    if (r < 0) continue;
+    const int64_t row = back_row[q];
+    if (r >= world || row < 0 || row >= capacity_rows) {
+      if (lane == 0) atomicCAS(err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(peer_bufs[r]) + row * row_vecs;
+    const uint4* s = src + q * row_vecs;
+    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(s + v);
+  }
+  __threadfence_system();
+}
+
+// Zero the padding rows (back_rank < 0) of a local receive buffer.
+__global__ void __launch_bounds__(kCopyThreads) zero_pad_rows_kernel(uint4* __restrict__ buf,
+                                                                     int64_t row_vecs,
+                                                                     const int32_t* __restrict__ back_rank,
+                                                                     int64_t m_pad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t q = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); q < m_pad;
+       q += warps) {
+    if (back_rank[q] >= 0) continue;
+    for (int64_t v = lane; v < row_vecs; v += 32) buf[q * row_vecs + v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+static int copy_grid(int64_t rows, int max_blocks) {
+  const int64_t want = (rows + (kCopyThreads / 32) - 1) / (kCopyThreads / 32);
+  const int64_t cap = max_blocks > 0 ? max_blocks : int64_t(num_sms()) * 8;
+  return int(std::max<int64_t>(1, std::min<int64_t>(want, cap)));
+}
+
+}  // namespace mxg
+
+using namespace mxg;
+
+extern "C" int mxg_peer_alloc(size_t bytes, void** dptr, void* handle_out) {
+  if (!dptr || !handle_out || bytes == 0) return MXG_ERR_INVALID_ARGUMENT;
+  int st = check_device();
+  if (st) return st;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MXG_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return MXG_ERR_CUDA;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == MXG_PEER_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *dptr = p;
+  return MXG_OK;
+}
+
+extern "C" int mxg_peer_open(const void* handle, void** dptr) {
+  if (!handle || !dptr) return MXG_ERR_INVALID_ARGUMENT;
+  int st = check_device();
+  if (st) return st;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MXG_ERR_CUDA;
+  *dptr = p;
+  return MXG_OK;
+}
+
+extern "C" int mxg_peer_close(void* dptr) {
+  if (!dptr) return MXG_ERR_INVALID_ARGUMENT;
+  return cuda_status(cudaIpcCloseMemHandle(dptr));
+}
+
+extern "C" int mxg_peer_free(void* dptr) {
+  if (!dptr) return MXG_ERR_INVALID_ARGUMENT;
+  return cuda_status(cudaFree(dptr));
+}
+
+extern "C" size_t mxg_ep_p2p_plan_workspace_size(int world, int num_slots) {
+  if (world < 1 || num_slots < 1) return 0;
+  return sizeof(int32_t) * (size_t(world) * (num_slots + 1) + 2 * size_t(num_slots)) + 256;
+}
+
+extern "C" int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slots, int me, int pad,
+                               int64_t m_pad, int32_t* slot_start, int32_t* dest_base,
+                               int32_t* group_rows, int32_t* group_start, int32_t* back_rank,
+                               int32_t* back_row, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (!counts_all || !slot_start || !dest_base || !group_rows || !group_start || !workspace)
+    return MXG_ERR_INVALID_ARGUMENT;
+  if (world < 1 || world > MXG_EP_MAX_RANKS || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
+      num_slots % world != 0 || me < 0 || me >= world || pad < 1 || m_pad < 0)
+    return MXG_ERR_INVALID_ARGUMENT;
+  if (m_pad > 0 && (!back_rank || !back_row)) return MXG_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < mxg_ep_p2p_plan_workspace_size(world, num_slots))
+    return MXG_ERR_WORKSPACE_TOO_SMALL;
+  int st = check_device();
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  int32_t* pref = reinterpret_cast<int32_t*>(workspace);
+  int32_t* gs = pref + size_t(world) * (num_slots + 1);
+  int32_t* tot = gs + num_slots;
+  p2p_plan_kernel<<<1, 512, 0, s>>>(counts_all, world, num_slots, me, pad, pref, gs, tot,
+                                    slot_start, dest_base, group_rows, group_start);
+  if (m_pad > 0)
+    p2p_back_kernel<<<num_slots / world, 256, 0, s>>>(counts_all, world, num_slots, me, pad, pref,
+                                                      gs, tot, back_rank, back_row);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
+                                   int64_t n_send, const int32_t* slot_start,
+                                   const int32_t* dest_base, int num_slots, int e_local,
+                                   const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
+                                   void* stream) {
+  if (n_send < 0 || row_bytes < 0 || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
+      e_local < 1 || num_slots % e_local != 0 || capacity_rows < 0)
+    return MXG_ERR_INVALID_ARGUMENT;
+  if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (n_send == 0 || row_bytes == 0) return MXG_OK;
+  if (!src || !send_rows || !slot_start || !dest_base || !peer_bufs) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(src)) return MXG_ERR_MISALIGNED;
+  int st = check_device();
+  if (st) return st;
+  int* err = device_error_word();
+  if (!err) return MXG_ERR_CUDA;
+  p2p_dispatch_kernel<<<copy_grid(n_send, max_blocks), kCopyThreads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint4*>(src), row_bytes / 16, send_rows, n_send, slot_start, dest_base,
+      num_slots, e_local, peer_bufs, capacity_rows, err);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* back_rank,
+                                 const int32_t* back_row, int64_t m_pad, const uint64_t* peer_bufs,
+                                 int world, int64_t capacity_rows, int max_blocks, void* stream) {
+  if (m_pad < 0 || row_bytes < 0 || world < 1 || capacity_rows < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (m_pad == 0 || row_bytes == 0) return MXG_OK;
+  if (!src || !back_rank || !back_row || !peer_bufs) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(src)) return MXG_ERR_MISALIGNED;
+  int st = check_device();
+  if (st) return st;
+  int* err = device_error_word();
+  if (!err) return MXG_ERR_CUDA;
+  p2p_return_kernel<<<copy_grid(m_pad, max_blocks), kCopyThreads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint4*>(src), row_bytes / 16, back_rank, back_row, m_pad, peer_bufs,
+      world, capacity_rows, err);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int mxg_ep_zero_pad_rows(void* buf, int64_t row_bytes, const int32_t* back_rank,
+                                    int64_t m_pad, void* stream) {
+  if (m_pad < 0 || row_bytes < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
+  if (m_pad == 0 || row_bytes == 0) return MXG_OK;
+  if (!buf || !back_rank) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(buf)) return MXG_ERR_MISALIGNED;
+  int st = check_device();
+  if (st) return st;
+  zero_pad_rows_kernel<<<copy_grid(m_pad, 0), kCopyThreads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<uint4*>(buf), row_bytes / 16, back_rank, m_pad);
+  return cuda_status(cudaGetLastError());
+}

@@ -24,6 +24,7 @@ there is no CPU path in the library.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -86,6 +87,116 @@ class CudaEpOps:
         return out
 
 
+class CudaP2POps:
+    """The NVLink peer-memory exchange kernels of libmxg.so (current stream)."""
+
+    def __init__(self):
+        self.L = _lib.load()
+
+    def plan(self, counts_all: torch.Tensor, me: int, pad: int, m_pad: int):
+        world, E = counts_all.shape
+        dev = counts_all.device
+        e_local = E // world
+        slot_start = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        dest_base = torch.empty(E, dtype=torch.int32, device=dev)
+        group_rows = torch.empty(e_local, dtype=torch.int32, device=dev)
+        group_start = torch.empty(e_local + 1, dtype=torch.int32, device=dev)
+        back_rank = torch.empty(max(m_pad, 1), dtype=torch.int32, device=dev)
+        back_row = torch.empty(max(m_pad, 1), dtype=torch.int32, device=dev)
+        ws = _lib.workspace(self.L.mxg_ep_p2p_plan_workspace_size(world, E), dev)
+        _lib.check(self.L.mxg_ep_p2p_plan(counts_all.contiguous().data_ptr(), world, E, me, pad, m_pad,
+                                          slot_start.data_ptr(), dest_base.data_ptr(),
+                                          group_rows.data_ptr(), group_start.data_ptr(),
+                                          back_rank.data_ptr(), back_row.data_ptr(), ws.data_ptr(),
+                                          ws.numel(), _lib.stream_ptr(dev)), "mxg_ep_p2p_plan")
+        return slot_start, dest_base, group_rows, group_start, back_rank[:m_pad], back_row[:m_pad]
+
+    def dispatch(self, src, send_rows, slot_start, dest_base, e_local, peer_ptrs, capacity_rows,
+                 max_blocks=0):
+        src = src.contiguous()
+        row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
+        _lib.check(self.L.mxg_ep_dispatch_p2p(src.data_ptr() if src.numel() else None, row_bytes,
+                                              send_rows.data_ptr(), send_rows.numel(),
+                                              slot_start.data_ptr(), dest_base.data_ptr(),
+                                              dest_base.numel(), e_local, peer_ptrs.data_ptr(),
+                                              capacity_rows, max_blocks,
+                                              _lib.stream_ptr(src.device)), "mxg_ep_dispatch_p2p")
+
+    def ret(self, src, back_rank, back_row, peer_ptrs, capacity_rows, max_blocks=0):
+        src = src.contiguous()
+        row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
+        _lib.check(self.L.mxg_ep_return_p2p(src.data_ptr() if src.numel() else None, row_bytes,
+                                            back_rank.data_ptr(), back_row.data_ptr(), back_rank.numel(),
+                                            peer_ptrs.data_ptr(), peer_ptrs.numel(), capacity_rows,
+                                            max_blocks, _lib.stream_ptr(src.device)),
+                   "mxg_ep_return_p2p")
+
+    def zero_pad_rows(self, buf, back_rank):
+        row_bytes = buf.element_size() * (buf[0].numel() if buf.shape[0] else 0)
+        _lib.check(self.L.mxg_ep_zero_pad_rows(buf.data_ptr() if buf.numel() else None, row_bytes,
+                                               back_rank.data_ptr(), back_rank.numel(),
+                                               _lib.stream_ptr(buf.device)), "mxg_ep_zero_pad_rows")
+
+
+class _CudaMem:
+    """A raw device range exposed through the CUDA array interface (no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+class PeerBuffer:
+    """A device buffer of this rank that every rank of the group can write
+    (CUDA IPC).  ``ptrs`` holds every rank's address of its own buffer, as
+    seen from this process; ``local`` is this rank's buffer as a uint8 tensor."""
+
+    def __init__(self, nbytes: int, group, world: int, rank: int, device: torch.device):
+        self.L = _lib.load()
+        self.rank, self.world = rank, world
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.check(self.L.mxg_peer_alloc(nbytes, ctypes.byref(own),
+                                         ctypes.cast(handle, ctypes.c_void_p)), "mxg_peer_alloc")
+        self.own = own.value
+        mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+        every = torch.empty(world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().view(world, 64)
+        self.opened = []
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self.own)
+                continue
+            h = (ctypes.c_uint8 * 64)(*every[r].tolist())
+            p = ctypes.c_void_p()
+            _lib.check(self.L.mxg_peer_open(ctypes.cast(h, ctypes.c_void_p), ctypes.byref(p)),
+                       "mxg_peer_open")
+            ptrs.append(p.value)
+            self.opened.append(p.value)
+        self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.nbytes = nbytes
+        self.local = torch.as_tensor(_CudaMem(self.own, nbytes), device=device)
+
+    def view(self, rows: int, like: torch.Tensor) -> torch.Tensor:
+        """This rank's buffer as [rows, *like.shape[1:]] of like.dtype."""
+        shape = (rows,) + tuple(like.shape[1:])
+        n = like.element_size()
+        for d in shape:
+            n *= d
+        return self.local[:n].view(like.dtype).view(shape)
+
+    def close(self):
+        for p in self.opened:
+            self.L.mxg_peer_close(ctypes.c_void_p(p))
+        self.opened = []
+        if self.own:
+            self.local = None
+            self.L.mxg_peer_free(ctypes.c_void_p(self.own))
+            self.own = None
+
+
 def balanced_placement(expert_load, world: int, refine_iters: int = 2000) -> np.ndarray:
     """slot_of_expert [E] with exactly E / world experts per rank and the
     expected rows per rank evened out: experts in decreasing load go to the
@@ -146,12 +257,23 @@ class DispatchPlan:
     recv_rows: int              # real (unpadded) rows received
     n_tokens: int
     topk: int
+    # NVLink peer-memory transport only
+    slot_start: torch.Tensor | None = None   # [E+1] send-position prefix over slots
+    dest_base: torch.Tensor | None = None    # [E] destination row of position p = dest_base[s] + p
+    back_rank: torch.Tensor | None = None    # [M_pad] home rank of each padded row (-1: padding)
+    back_row: torch.Tensor | None = None     # [M_pad] send position on that rank
 
 
 class ExpertParallel:
     """Dispatch/combine of routed token rows over a process group."""
 
-    def __init__(self, num_experts: int, group=None, pad: int = 32, ops=None, placement=None):
+    def __init__(self, num_experts: int, group=None, pad: int = 32, ops=None, placement=None,
+                 transport: str = "auto", max_tokens: int = 0, p2p_max_blocks: int = 0):
+        """transport: "p2p" (rows written straight into the owners' buffers
+        over NVLink, ranks of one node), "nccl" (all_to_all_single), or "auto"
+        (p2p on CUDA with more than one rank).  max_tokens sizes the p2p
+        receive buffers for batches up to that many tokens per rank (they
+        grow on demand, collectively, when a larger batch arrives)."""
         self.group = group
         self.world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -168,6 +290,46 @@ class ExpertParallel:
             if p.shape != (num_experts,) or not np.array_equal(np.sort(p), np.arange(num_experts)):
                 raise ValueError("placement must be a permutation of the expert ids")
             self.placement = p
+        if transport not in ("auto", "p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        if transport == "auto":
+            transport = "p2p" if (self.world > 1 and torch.cuda.is_available() and ops is None) else "nccl"
+        self.transport = transport
+        self.p2p = CudaP2POps() if transport == "p2p" else None
+        self.max_tokens = max_tokens
+        self.p2p_max_blocks = p2p_max_blocks
+        self.buffers = {}        # name -> PeerBuffer
+        self.capacity = {}       # name -> rows
+        self._flag = None
+
+    def close(self):
+        """Release the peer buffers (collective: every rank calls it)."""
+        if self.buffers:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            for b in self.buffers.values():
+                b.close()
+            self.buffers, self.capacity = {}, {}
+
+    def _barrier(self, device):
+        """Stream-ordered rendezvous: returns on the device once every rank's
+        preceding kernels (and their peer stores) have completed."""
+        if self._flag is None or self._flag.device != device:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _ensure_buffer(self, name, rows, row_bytes, device):
+        """Collective when it (re)allocates: every rank decides from the same
+        all-gathered counts."""
+        if self.capacity.get(name, (0, 0))[0] >= rows and self.capacity[name][1] == row_bytes:
+            return
+        old = self.buffers.pop(name, None)
+        if old is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            old.close()
+        self.buffers[name] = PeerBuffer(max(rows, 1) * row_bytes, self.group, self.world, self.rank, device)
+        self.capacity[name] = (max(rows, 1), row_bytes)
 
     def local_experts(self) -> list:
         """Global expert id held in each local slot of this rank."""
@@ -195,6 +357,8 @@ class ExpertParallel:
                 self.slot_of_expert = torch.from_numpy(self.placement).to(expert_ids.device)
             slot_map = self.slot_of_expert
         counts, send_rows, slot_pos = self.ops.route(expert_ids, self.num_experts, slot_map)
+        if self.transport == "p2p":
+            return self._dispatch_p2p(x, n, k, counts, send_rows, slot_pos)
         recv_counts = self._a2a(counts, counts.numel()).view(self.world, self.e_local)
         host = torch.cat([counts, recv_counts.reshape(-1)]).cpu().view(2, self.world, self.e_local)
         sc = host[0].sum(1).tolist()
@@ -209,8 +373,51 @@ class ExpertParallel:
                             n_recv, n, k)
         return self.dispatch_like(x, plan), plan
 
-    def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan) -> torch.Tensor:
-        """Rows of x [n, H'] moved along an existing plan (same routing)."""
+    def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos):
+        E, W, El, pad = self.num_experts, self.world, self.e_local, self.pad
+        C = torch.empty(W * E, dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(C, counts, group=self.group)   # also: every receiver is idle
+        C = C.view(W, E)
+        Ch = C.cpu().numpy().astype(np.int64)
+        tot = Ch.sum(0).reshape(W, El)                             # rows per (owner, local slot)
+        padded = (tot + pad - 1) // pad * pad
+        m_pad_all = padded.sum(1)
+        m_pad = int(m_pad_all[self.rank])
+        recv_rows = int(tot[self.rank].sum())
+        sent = Ch.sum(1)                                           # rows each rank sends
+        row_bytes = x.element_size() * (x[0].numel() if x.shape[0] else int(np.prod(x.shape[1:])))
+        n_cap = max(int(sent.max()) // max(k, 1), self.max_tokens)
+        worst = W * n_cap * min(k, El) + El * (pad - 1)
+        need = max(int(m_pad_all.max()), 1)
+        for name in ("x", "dy"):
+            if self.capacity.get(name, (0, 0))[0] < need:
+                self._ensure_buffer(name, max(worst, need), row_bytes, x.device)
+        if self.capacity.get("ret", (0, 0))[0] < int(sent.max()):
+            self._ensure_buffer("ret", max(n_cap * k, int(sent.max())), row_bytes, x.device)
+        slot_start, dest_base, group_rows, _, back_rank, back_row = self.p2p.plan(C, self.rank, pad, m_pad)
+        send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
+        recv_splits = Ch[:, self.rank * El:(self.rank + 1) * El].sum(1).tolist()
+        plan = DispatchPlan(send_rows, slot_pos, send_splits, recv_splits, None, None,
+                            group_rows, padded[self.rank].tolist(), recv_rows, n, k,
+                            slot_start, dest_base, back_rank, back_row)
+        return self.dispatch_like(x, plan, "x"), plan
+
+    def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy") -> torch.Tensor:
+        """Rows of x [n, H'] moved along an existing plan (same routing).  With
+        the p2p transport the result lives in the named receive buffer ("x" is
+        the one ``dispatch`` fills) until the next exchange into it."""
+        if plan.back_rank is not None:
+            m_pad = plan.back_rank.numel()
+            buf = self.buffers[buffer]
+            rows, row_bytes = self.capacity[buffer]
+            if x.shape[0] and x.element_size() * x[0].numel() != row_bytes:
+                raise ValueError("row size differs from the receive buffer's")
+            local = buf.view(m_pad, x)
+            self.p2p.zero_pad_rows(local, plan.back_rank)
+            self.p2p.dispatch(x, plan.send_rows, plan.slot_start, plan.dest_base, self.e_local,
+                              buf.ptrs, rows, self.p2p_max_blocks)
+            self._barrier(x.device)
+            return local
         send_buf = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
         recv_buf = self._a2a(send_buf, plan.recv_rows, plan.recv_splits, plan.send_splits)
         return self.ops.gather(recv_buf, plan.idx, plan.idx.numel())
@@ -218,6 +425,13 @@ class ExpertParallel:
     def combine(self, y_local: torch.Tensor, plan: DispatchPlan, weights=None) -> torch.Tensor:
         """y_local [M_pad, H'] results in the dispatch layout -> [n, H'] =
         sum over each token's choices (weighted when weights [n, k] given)."""
+        if plan.back_rank is not None:
+            buf = self.buffers["ret"]
+            rows, row_bytes = self.capacity["ret"]
+            self.p2p.ret(y_local, plan.back_rank, plan.back_row, buf.ptrs, rows, self.p2p_max_blocks)
+            self._barrier(y_local.device)
+            ret = buf.view(plan.n_tokens * plan.topk, y_local)
+            return self.ops.combine(ret, plan.slot_pos, weights, plan.n_tokens, plan.topk)
         back_buf = self.ops.gather(y_local, plan.back, plan.recv_rows)
         ret = self._a2a(back_buf, plan.n_tokens * plan.topk, plan.send_splits, plan.recv_splits)
         return self.ops.combine(ret, plan.slot_pos, weights, plan.n_tokens, plan.topk)

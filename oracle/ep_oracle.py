@@ -125,3 +125,39 @@ def simulate_combine(ys, routed, send_counts, plans, weights, ns, k):
         ret = np.concatenate(pieces[s])
         res.append(combine(ret, routed[s][2], weights[s], ns[s], k))
     return res
+
+
+def p2p_plan(counts_all: np.ndarray, me: int, pad: int = 32):
+    """The peer-memory exchange tables of rank ``me`` from the all-gathered
+    slot counts C [world, E]: the owners' receive buffers use the regroup
+    layout above, so send position p of slot s lands on rank s // E_local at
+    row dest_base[s] + p, and padded row q of ``me`` returns to
+    (back_rank[q], back_row[q])."""
+    C = np.asarray(counts_all, dtype=np.int64)
+    W, E = C.shape
+    El = E // W
+    tot = C.sum(0)
+    padded = (tot + pad - 1) // pad * pad
+    gs = np.zeros(E, np.int64)
+    for d in range(W):
+        gs[d * El:(d + 1) * El] = np.concatenate([[0], np.cumsum(padded[d * El:(d + 1) * El])[:-1]])
+    pref = np.concatenate([np.zeros((W, 1), np.int64), np.cumsum(C, axis=1)], axis=1)  # [W, E+1]
+    src_off = C[:me].sum(0)
+    dest_base = gs + src_off - pref[me, :E]
+    mine = slice(me * El, (me + 1) * El)
+    group_rows = padded[mine]
+    group_start = np.concatenate([gs[mine], [padded[mine].sum()]])
+    m_pad = int(padded[mine].sum())
+    back_rank = np.full(m_pad, -1, np.int64)
+    back_row = np.full(m_pad, -1, np.int64)
+    for le in range(El):
+        s = me * El + le
+        q = gs[s]
+        for r in range(W):
+            c = C[r, s]
+            back_rank[q:q + c] = r
+            back_row[q:q + c] = pref[r, s] + np.arange(c)
+            q += c
+    i32 = lambda a: np.asarray(a, dtype=np.int32)
+    return (i32(pref[me]), i32(dest_base), i32(group_rows), i32(group_start), i32(back_rank),
+            i32(back_row))

@@ -60,3 +60,12 @@ def test_host_validation_without_gpu(mxg):
     assert L.mxg_grouped_wgrad(16, None, 16, None, 16, 2, 2, 2, 100, 64, 64, 16, 0, 16, 1 << 20, None) == 2
     assert L.mxg_debug_inject_stall(-1) == 1
     assert L.mxg_debug_inject_stall(0) == 0
+
+
+def test_status_codes_match_header(mxg):
+    import re
+    text = open(mxg._lib.HEADER_PATH).read()
+    codes = dict(re.findall(r"#define (MXG_(?:OK|ERR_\w+))\s+(\d+)", text))
+    assert codes, "no status codes found in the header"
+    for name, value in codes.items():
+        assert getattr(mxg._lib, name) == int(value), name

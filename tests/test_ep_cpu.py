@@ -134,3 +134,33 @@ def test_expert_parallel_gloo(world, balanced):
         p.join(timeout=60)
     for r in range(world):
         assert res[r] == "ok", res[r]
+
+
+@pytest.mark.parametrize("world", [1, 3, 4])
+def test_p2p_plan_places_rows_like_regroup(world):
+    """Every send position lands where the regroup layout puts it, and every
+    padded row returns to its own send position."""
+    E, k, H = 4 * world, 3, 16
+    xs, ids = [], []
+    for r in range(world):
+        i, x, _ = make_rank_inputs(r, [40, 0, 77, 5][r], k, E, H, zipf=1.1)
+        xs.append(x), ids.append(i)
+    out, routed, send_counts = ep_oracle.simulate(xs, ids, E)
+    C = np.stack([rt[0] for rt in routed])
+    bufs = [np.zeros_like(o[0]) for o in out]
+    for r in range(world):
+        slot_start, dest_base, *_ = ep_oracle.p2p_plan(C, r)
+        sr = routed[r][1]
+        for p in range(sr.size):
+            s = int(np.searchsorted(slot_start, p, side="right") - 1)
+            bufs[s // (E // world)][dest_base[s] + p] = xs[r][sr[p]]
+    for d in range(world):
+        assert np.array_equal(bufs[d], out[d][0])
+        _, _, gr, gst, brank, brow = ep_oracle.p2p_plan(C, d)
+        assert np.array_equal(gr, out[d][2]["group_rows"])
+        for q in range(brank.size):
+            if brank[q] >= 0:
+                r, p = brank[q], brow[q]
+                assert np.array_equal(xs[r][routed[r][1][p]], out[d][0][q])
+            else:
+                assert np.all(out[d][0][q] == 0)

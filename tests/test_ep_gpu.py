@@ -142,7 +142,72 @@ def test_expert_layer_through_dispatch(mxg, orc, cuda_dev):
     assert err <= 1e-2 and orc.rel_frobenius(y_local.float().cpu().numpy(), ref_local) <= 1e-3
 
 
-def _nccl_worker(rank, world, port, q):
+@pytest.mark.parametrize("world,k,H", [(4, 3, 1024), (2, 8, 7168), (1, 2, 256)])
+def test_p2p_kernels_emulated_ranks(mxg, cuda_dev, world, k, H):
+    """The peer-memory plan, dispatch and return kernels with every rank's
+    buffers on one GPU (the kernels only store; nothing waits on a peer):
+    received rows equal the regroup layout bit for bit, and returned rows
+    combine to the oracle's result."""
+    E = 4 * world
+    ns = [300, 0, 517, 64][:world]
+    ins = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
+    xs = [_bf16(a[1], cuda_dev) for a in ins]
+    ep = mxg.ep.CudaEpOps()
+    p2p = mxg.ep.CudaP2POps()
+    routed = [ep.route(torch.from_numpy(a[0]).to(cuda_dev), E) for a in ins]
+    C = torch.stack([rt[0] for rt in routed])
+    out, orouted, osc = ep_oracle.simulate([x.float().cpu().numpy() for x in xs], [a[0] for a in ins], E)
+    cap = max(o[0].shape[0] for o in out) + 7
+    bufs = [torch.full((cap, H), 7.0, dtype=torch.bfloat16, device=cuda_dev) for _ in range(world)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=cuda_dev)
+    plans = []
+    for r in range(world):
+        m_pad = out[r][0].shape[0]
+        pl = p2p.plan(C, r, 32, m_pad)
+        want = ep_oracle.p2p_plan(C.cpu().numpy(), r)
+        for got, w in zip(pl, want):
+            assert np.array_equal(got.cpu().numpy(), w)
+        plans.append(pl)
+        p2p.zero_pad_rows(bufs[r][:m_pad], pl[4])
+    for r in range(world):
+        p2p.dispatch(xs[r], routed[r][1], plans[r][0], plans[r][1], E // world, ptrs, cap)
+    for d in range(world):
+        m_pad = out[d][0].shape[0]
+        assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), out[d][0])
+    assert mxg.device_error() == 0
+    # return: every padded row goes home, then the weighted combine
+    ret_rows = max(ns) * k   # every rank's return buffer has the same capacity
+    rets = [torch.zeros(ret_rows, H, dtype=torch.bfloat16, device=cuda_dev) for r in range(world)]
+    rptrs = torch.tensor([t.data_ptr() for t in rets], dtype=torch.int64, device=cuda_dev)
+    for d in range(world):
+        m_pad = out[d][0].shape[0]
+        p2p.ret(bufs[d][:m_pad], plans[d][4], plans[d][5], rptrs, ret_rows)
+    for r in range(world):
+        if ns[r] == 0:
+            continue
+        w = ins[r][2]
+        y = ep.combine(rets[r][:ns[r] * k], routed[r][2], torch.from_numpy(w).to(cuda_dev), ns[r], k)
+        rows = xs[r].float().cpu().numpy()[orouted[r][1]]
+        assert combine_close(y.float().cpu().numpy(), rows, orouted[r][2], w, ns[r], k)
+
+
+def test_p2p_dispatch_rejects_rows_past_capacity(mxg, cuda_dev):
+    """A destination row outside the buffer is skipped and reported, not written."""
+    E, k, H = 4, 2, 64
+    ids, x, _ = make_rank_inputs(0, 100, k, E, H)
+    ep, p2p = mxg.ep.CudaEpOps(), mxg.ep.CudaP2POps()
+    c, sr, sp = ep.route(torch.from_numpy(ids).to(cuda_dev), E)
+    C = c.view(1, E)
+    pl = p2p.plan(C, 0, 32, int(((c.cpu().numpy() + 31) // 32 * 32).sum()))
+    small = torch.zeros(8, H, dtype=torch.bfloat16, device=cuda_dev)
+    guard = torch.zeros(64, H, dtype=torch.bfloat16, device=cuda_dev)
+    ptrs = torch.tensor([small.data_ptr()], dtype=torch.int64, device=cuda_dev)
+    p2p.dispatch(_bf16(x, cuda_dev), sr, pl[0], pl[1], E, ptrs, 8)
+    assert mxg.device_error() == mxg._lib.MXG_ERR_WORKSPACE_TOO_SMALL
+    assert torch.all(guard == 0)
+
+
+def _nccl_worker(rank, world, port, q, transport="nccl"):
     try:
         import datetime
         import torch.distributed as dist
@@ -155,7 +220,7 @@ def _nccl_worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         E, k, H = 16, 8, 1024
         ns = [2048, 512]
-        par = mxg.ExpertParallel(E)
+        par = mxg.ExpertParallel(E, transport=transport)
         all_in = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
         ids, x, w = all_in[rank]
         xb = _bf16(x, dev)
@@ -166,22 +231,30 @@ def _nccl_worker(rank, world, port, q):
         y = par.combine(x_local, plan, torch.from_numpy(w).to(dev))
         rows = xs[rank][routed[rank][1]]
         ok2 = combine_close(y.float().cpu().numpy(), rows, routed[rank][2], w, ns[rank], k)
+        # a second step with other tokens reuses the buffers
+        x2 = _bf16(x * 3, dev)
+        x_local2, plan2 = par.dispatch(x2, torch.from_numpy(ids).to(dev))
+        ok3 = np.array_equal(x_local2.float().cpu().numpy(),
+                             ep_oracle.simulate([torch.from_numpy(a[1] * 3).to(torch.bfloat16).float().numpy()
+                                                 for a in all_in], [a[0] for a in all_in], E)[0][rank][0])
         torch.cuda.synchronize()
+        par.close()
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, "ok" if ok and ok2 else f"dispatch {ok} combine {ok2}"))
+        q.put((rank, "ok" if ok and ok2 and ok3 else f"dispatch {ok} combine {ok2} second {ok3}"))
     except Exception:
         import traceback
         q.put((rank, traceback.format_exc()))
 
 
-def test_expert_parallel_nccl_world2():
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_expert_parallel_world2(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
