@@ -150,15 +150,17 @@ __global__ void __launch_bounds__(kColThreads) quant_colwise_kernel(
 // One pass over a bf16 tensor [rows, cols] (rows a multiple of 32) producing
 // the row-wise (1x32) and/or the column-wise (32x1, transposed) encodings,
 // each bit-identical to the dedicated kernels above.  A block owns a tile of
-// 32 rows x 256 columns: every thread takes four 16-byte chunks (a warp reads
-// one 512-byte row segment), encodes them row-wise in registers (four lanes
-// per 32-element block, as the row-wise kernel), parks them in shared memory,
-// and after a barrier each thread encodes one tile column (32 rows) for the
-// transposed output.  The tensor may be computed on the fly from its inputs
+// 64 rows x 256 columns: every thread issues eight 16-byte loads at once (a
+// warp reads one 512-byte row segment each), encodes the chunks row-wise in
+// registers (four lanes per 32-element block, as the row-wise kernel), parks
+// them in shared memory, and after a barrier each thread encodes two tile
+// columns over 32 rows for the transposed output (the two row halves of a
+// column write adjacent 32-byte runs).  The tensor may be computed on the fly from its inputs
 // (SwiGLU, and the SwiGLU gradient), rounded to bf16 exactly as the unfused
 // kernels round their outputs, so it is never written to memory.
 enum { DUAL_PLAIN = 0, DUAL_SWIGLU = 1, DUAL_SWIGLU_GRAD = 2 };
-constexpr int kTileCols = 256;
+constexpr int kTileRows = 128;                // 32 KiB tiles: kTileRows x kTileCols bf16
+constexpr int kTileCols = 16384 / kTileRows;
 
 struct DualArgs {
   const uint4* a;    // x (plain) or gu (swiglu variants), rows of 16-byte chunks
@@ -222,96 +224,139 @@ __device__ __forceinline__ void encode_row_chunk(const DualArgs& a, uint4 v, int
 }
 
 template <int KIND>
-__global__ void __launch_bounds__(256) quant_dual_kernel(DualArgs a) {
-  __shared__ __align__(16) uint16_t tile[32][kTileCols];
-  const int64_t r0 = int64_t(blockIdx.y) * 32;
+__global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
+  constexpr int R = kTileRows, CW = kTileCols / 2;      // tile rows, tile width in bf16x2 words
+  constexpr int CPR = kTileCols / 8;                     // 16-byte chunks per tile row
+  __shared__ __align__(16) uint32_t tile[R][CW];
+  const int64_t r0 = int64_t(blockIdx.y) * R;
   const int t = threadIdx.x;
   // tile columns -> tensor columns: contiguous, except for the gradient where
-  // tile columns [0,128) are dg[j0 + c] and [128,256) are du[j0 + c - 128]
+  // the first half of the tile is dg[j0 + c] and the second du[j0 + c]
   const int64_t c0 = KIND == DUAL_SWIGLU_GRAD ? int64_t(blockIdx.x) * (kTileCols / 2)
                                               : int64_t(blockIdx.x) * kTileCols;
   if (KIND != DUAL_SWIGLU_GRAD) {
+    uint4 v[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = t + 256 * i;          // chunk of the tile: row k / 32, chunk k % 32
-      const int r = k >> 5, ch = k & 31;
+    for (int i = 0; i < 8; ++i) {  // all loads first: 128 bytes in flight per thread
+      const int k = t + 256 * i;
+      const int r = k / CPR, ch = k % CPR;
       const int64_t col = c0 + ch * 8;
-      const bool valid = col < a.cols;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (valid) {
+      v[i] = make_uint4(0, 0, 0, 0);
+      if (col < a.cols && r0 + r < a.rows) {
         if (KIND == DUAL_PLAIN) {
-          v = __ldcs(a.a + ((r0 + r) * a.cols + col) / 8);
+          v[i] = __ldcs(a.a + ((r0 + r) * a.cols + col) / 8);
         } else {
           const uint4* rowp = a.a + (r0 + r) * (2 * a.inter) / 8;
-          v = swiglu_chunk(__ldcs(rowp + col / 8), __ldcs(rowp + (a.inter + col) / 8));
+          v[i] = swiglu_chunk(__ldcs(rowp + col / 8), __ldcs(rowp + (a.inter + col) / 8));
         }
       }
-      if (a.q) encode_row_chunk(a, v, r0 + r, col, valid);
-      *reinterpret_cast<uint4*>(&tile[r][ch * 8]) = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int k = t + 256 * i;
+      const int r = k / CPR, ch = k % CPR;
+      const int64_t col = c0 + ch * 8;
+      const bool valid = col < a.cols && r0 + r < a.rows;
+      if (a.q) encode_row_chunk(a, v[i], r0 + r, col, valid);
+      *reinterpret_cast<uint4*>(&tile[r][ch * 4]) = v[i];
     }
   } else {
+    constexpr int JCPR = CPR / 2;  // input chunks per tile row (each yields a dg and a du chunk)
+    uint4 dg[4], du[4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int k = t + 256 * i;          // input chunk: row k / 16, j-chunk k % 16
-      const int r = k >> 4, ch = k & 15;
+    for (int i = 0; i < 4; ++i) {
+      const int k = t + 256 * i;
+      const int r = k / JCPR, ch = k % JCPR;
       const int64_t j = c0 + ch * 8;
-      const bool valid = j < a.inter;
-      uint4 dg = make_uint4(0, 0, 0, 0), du = dg;
-      if (valid) {
+      dg[i] = make_uint4(0, 0, 0, 0);
+      du[i] = dg[i];
+      if (j < a.inter && r0 + r < a.rows) {
         const uint4* rowp = a.a + (r0 + r) * (2 * a.inter) / 8;
         const uint4 g = __ldcs(rowp + j / 8), u = __ldcs(rowp + (a.inter + j) / 8);
         const uint4 d = __ldcs(a.dh + ((r0 + r) * a.inter + j) / 8);
-        swiglu_grad_word(g.x, u.x, d.x, dg.x, du.x);
-        swiglu_grad_word(g.y, u.y, d.y, dg.y, du.y);
-        swiglu_grad_word(g.z, u.z, d.z, dg.z, du.z);
-        swiglu_grad_word(g.w, u.w, d.w, dg.w, du.w);
+        swiglu_grad_word(g.x, u.x, d.x, dg[i].x, du[i].x);
+        swiglu_grad_word(g.y, u.y, d.y, dg[i].y, du[i].y);
+        swiglu_grad_word(g.z, u.z, d.z, dg[i].z, du[i].z);
+        swiglu_grad_word(g.w, u.w, d.w, dg[i].w, du[i].w);
       }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = t + 256 * i;
+      const int r = k / JCPR, ch = k % JCPR;
+      const int64_t j = c0 + ch * 8;
+      const bool valid = j < a.inter && r0 + r < a.rows;
       if (a.q) {
-        encode_row_chunk(a, dg, r0 + r, j, valid);
-        encode_row_chunk(a, du, r0 + r, a.inter + j, valid);
+        encode_row_chunk(a, dg[i], r0 + r, j, valid);
+        encode_row_chunk(a, du[i], r0 + r, a.inter + j, valid);
       }
-      *reinterpret_cast<uint4*>(&tile[r][ch * 8]) = dg;
-      *reinterpret_cast<uint4*>(&tile[r][128 + ch * 8]) = du;
+      *reinterpret_cast<uint4*>(&tile[r][ch * 4]) = dg[i];
+      *reinterpret_cast<uint4*>(&tile[r][CW / 2 + ch * 4]) = du[i];
     }
   }
   if (a.qt == nullptr) return;
   __syncthreads();
-  // column pass: thread t encodes tile column t over the 32 rows
-  int64_t col;
+  // column pass: thread t encodes tile columns 2p, 2p+1 (p = t % CW) over the
+  // 32 rows of row block t / CW; the row blocks of a column write adjacent
+  // 32-byte runs of the transposed output
+  const int pcol = t % CW, rblk = t / CW;
+  if (r0 + 32 * rblk >= a.rows) return;
+  int64_t col0;
   if (KIND == DUAL_SWIGLU_GRAD) {
-    const int64_t j = c0 + (t & 127);
+    const int64_t j = c0 + 2 * (pcol % (CW / 2));
     if (j >= a.inter) return;
-    col = t < 128 ? j : a.inter + j;
+    col0 = pcol < CW / 2 ? j : a.inter + j;
   } else {
-    col = c0 + t;
-    if (col >= a.cols) return;
+    col0 = c0 + 2 * pcol;
+    if (col0 >= a.cols) return;
   }
-  uint32_t w[16];  // rows 2i (low half) and 2i+1 (high half)
-  uint32_t m = 0;
+  // two passes over shared memory (amax, then encode) keep few registers live
+  const uint32_t* colp = &tile[32 * rblk][pcol];
+  uint32_t m0 = 0, m1 = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    w[i] = uint32_t(tile[2 * i][t]) | (uint32_t(tile[2 * i + 1][t]) << 16);
-    m = max(m, amax2(w[i]));
+  for (int r = 0; r < 32; ++r) {
+    const uint32_t wr = colp[r * CW];
+    m0 = max(m0, wr & 0x7FFFu);
+    m1 = max(m1, (wr >> 16) & 0x7FFFu);
   }
-  const uint32_t b = rceil_byte(m);
-  const float f = descale_of(b);
-  uint32_t out[8];
+  const uint32_t b0 = rceil_byte(m0), b1 = rceil_byte(m1);
+  const float f0 = descale_of(b0), f1 = descale_of(b1);
+  const int64_t rb = r0 + 32 * rblk;
+  uint4* d0 = reinterpret_cast<uint4*>(a.qt + col0 * a.rows + rb);
+  uint4* d1 = reinterpret_cast<uint4*>(a.qt + (col0 + 1) * a.rows + rb);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint32_t lo = cvt_e4m3x2(bf16_lo(w[2 * j]) * f, bf16_hi(w[2 * j]) * f);
-    uint32_t hi = cvt_e4m3x2(bf16_lo(w[2 * j + 1]) * f, bf16_hi(w[2 * j + 1]) * f);
-    if (b == 255u) {
-      lo = fix_nan_byte(lo & 0xFFu, w[2 * j] & 0xFFFFu) |
-           (fix_nan_byte((lo >> 8) & 0xFFu, w[2 * j] >> 16) << 8);
-      hi = fix_nan_byte(hi & 0xFFu, w[2 * j + 1] & 0xFFFFu) |
-           (fix_nan_byte((hi >> 8) & 0xFFu, w[2 * j + 1] >> 16) << 8);
+  for (int hh = 0; hh < 2; ++hh) {  // rows [16hh, 16hh + 16): one 16-byte store per column
+    uint32_t o0[4], o1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) w4[q] = colp[(16 * hh + 4 * j + q) * CW];
+      const uint32_t a01 = cvt_e4m3x2(bf16_lo(w4[0]) * f0, bf16_lo(w4[1]) * f0);
+      const uint32_t a23 = cvt_e4m3x2(bf16_lo(w4[2]) * f0, bf16_lo(w4[3]) * f0);
+      const uint32_t b01 = cvt_e4m3x2(bf16_hi(w4[0]) * f1, bf16_hi(w4[1]) * f1);
+      const uint32_t b23 = cvt_e4m3x2(bf16_hi(w4[2]) * f1, bf16_hi(w4[3]) * f1);
+      o0[j] = a01 | (a23 << 16);
+      o1[j] = b01 | (b23 << 16);
+      if (b0 == 255u || b1 == 255u) {
+        uint32_t p0 = 0, p1 = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t x0 = (o0[j] >> (8 * q)) & 0xFFu, x1 = (o1[j] >> (8 * q)) & 0xFFu;
+          if (b0 == 255u) x0 = fix_nan_byte(x0, w4[q] & 0xFFFFu);
+          if (b1 == 255u) x1 = fix_nan_byte(x1, w4[q] >> 16);
+          p0 |= x0 << (8 * q);
+          p1 |= x1 << (8 * q);
+        }
+        o0[j] = p0;
+        o1[j] = p1;
+      }
     }
-    out[j] = lo | (hi << 16);
+    __stcs(d0 + hh, make_uint4(o0[0], o0[1], o0[2], o0[3]));
+    __stcs(d1 + hh, make_uint4(o1[0], o1[1], o1[2], o1[3]));
   }
-  uint4* d = reinterpret_cast<uint4*>(a.qt + col * a.rows + r0);
-  __stcs(d, make_uint4(out[0], out[1], out[2], out[3]));
-  __stcs(d + 1, make_uint4(out[4], out[5], out[6], out[7]));
-  a.st[col * (a.rows / 32) + blockIdx.y] = uint8_t(b);
+  a.st[col0 * (a.rows / 32) + rb / 32] = uint8_t(b0);
+  a.st[(col0 + 1) * (a.rows / 32) + rb / 32] = uint8_t(b1);
 }
 
 template <int KIND>
@@ -323,12 +368,12 @@ static int launch_dual(DualArgs a, void* stream) {
   if (a.rows % 32 != 0 || a.cols % 32 != 0) return MXG_ERR_BAD_SHAPE;
   if ((a.q && !aligned16(a.q)) || (a.qt && !aligned16(a.qt))) return MXG_ERR_MISALIGNED;
   if (a.rows == 0 || a.cols == 0) return MXG_OK;
-  if (a.rows / 32 > 65535) return MXG_ERR_BAD_SHAPE;
+  if ((a.rows + kTileRows - 1) / kTileRows > 65535) return MXG_ERR_BAD_SHAPE;
   int e = check_device();
   if (e) return e;
   const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
   const int64_t per = KIND == DUAL_SWIGLU_GRAD ? kTileCols / 2 : kTileCols;
-  dim3 grid(unsigned((span + per - 1) / per), unsigned(a.rows / 32));
+  dim3 grid(unsigned((span + per - 1) / per), unsigned((a.rows + kTileRows - 1) / kTileRows));
   quant_dual_kernel<KIND><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
   return cuda_status(cudaGetLastError());
 }
