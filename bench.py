@@ -404,7 +404,7 @@ class EpLayerBench:
     gradients and its local experts."""
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
-                 transport="auto", p2p_blocks=0):
+                 transport="auto", p2p_blocks=0, reserve_sms=0):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -426,7 +426,8 @@ class EpLayerBench:
         w_gu = torch.randn(e_loc, GATE_UP, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
         w_d = torch.randn(e_loc, HIDDEN, INTER, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
         self.comm = torch.cuda.Stream() if (overlap and world > 1) else None
-        self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm)
+        self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm,
+                                     reserve_sms=reserve_sms)
         del w_gu, w_d
         torch.cuda.synchronize()
 
@@ -533,14 +534,15 @@ def measure_ep_layer(lb, world, steps, warmup):
                          "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
                          "peak_source": pk["source"], "traffic": None,
                          "flops_per_launch": flops[dom]},
-            "placement": lb.placement, "overlap": lb.comm is not None, "transport": lb.ep.transport}
+            "placement": lb.placement, "overlap": lb.comm is not None, "transport": lb.ep.transport,
+            "reserve_sms": lb.layer.reserve}
 
 
 def run_ep_mxg(args, rank, world, local):
     """The N>1 bench line: config 5 across the process group."""
     pkg()._lib.load()
-    lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=not args.no_overlap,
-                      transport=args.transport, p2p_blocks=args.p2p_blocks)
+    lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
+                      transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -559,6 +561,7 @@ def run_ep_mxg(args, rank, world, local):
                       "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
                       "hidden": HIDDEN, "intermediate": INTER, "placement": r["placement"],
                       "comm_overlap": r["overlap"], "transport": r["transport"],
+                      "reserved_sms": r["reserve_sms"],
                       "parallelism": f"ep{world}",
                       "l2": "operands > L2 (no flush needed)"},
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
@@ -812,11 +815,15 @@ def main():
                     help="small: reduced problem for profiler captures (not a bench line)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement for the EP layer (N>1)")
-    ap.add_argument("--no-overlap", action="store_true", help="EP layer: collectives on the main stream")
+    ap.add_argument("--overlap", action="store_true",
+                    help="EP layer: run the dy dispatch and the combine's return beside the GEMMs "
+                         "(measured slower on 8 B200s: the GEMMs lose more than the exchange hides)")
     ap.add_argument("--no-ep", action="store_true", help="N=1: skip the one-GPU EP layer measurement")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
                     help="EP layer token exchange: NVLink peer stores or NCCL all_to_all")
     ap.add_argument("--p2p-blocks", type=int, default=0, help="grid cap of the peer-store kernels (0: default)")
+    ap.add_argument("--reserve-sms", type=int, default=0,
+                    help="EP layer with --overlap: SMs kept free of GEMM blocks for the peer copies")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

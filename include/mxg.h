@@ -245,33 +245,46 @@ MXG_API int mxg_peer_free(void* dptr);
  * rank s / (num_slots / world)): this rank's send-position prefix
  * slot_start [num_slots + 1], dest_base [num_slots] (destination row of send
  * position p in slot s = dest_base[s] + p), its own padded groups
- * group_rows / group_start [e_local (+1)], and for each of its m_pad padded
- * rows the rank and send position the result returns to (back_rank,
- * back_row; -1 on padding rows). */
+ * group_rows / group_start [e_local (+1)], for each of its m_pad padded rows
+ * the rank and send position the result returns to (back_rank, back_row; -1
+ * on padding rows), and ret_order: its real rows grouped by home rank in the
+ * order me+1, me+2, ... (mod world). */
 MXG_API size_t mxg_ep_p2p_plan_workspace_size(int world, int num_slots);
 MXG_API int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slots, int me, int pad,
                             int64_t m_pad, int32_t* slot_start, int32_t* dest_base,
                             int32_t* group_rows, int32_t* group_start, int32_t* back_rank,
-                            int32_t* back_row, void* workspace, size_t workspace_bytes, void* stream);
+                            int32_t* back_row, int32_t* ret_order, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* Row src[send_rows[p]] -> row dest_base[s] + p of peer_bufs[s / e_local]
- * (peer_bufs: device array of every rank's buffer address).  A destination
- * row outside [0, capacity_rows) is skipped and sets the device error word.
- * max_blocks <= 0: the library's default grid. */
+ * (peer_bufs: device array of every rank's buffer address), starting with
+ * the positions bound for rank me+1 so that the ranks write to different
+ * peers at the same time.  A destination row outside [0, capacity_rows) is
+ * skipped and sets the device error word.  max_blocks <= 0: the library's
+ * default grid, sharing SMs with concurrent work; max_blocks > 0: that many
+ * 1024-thread blocks that only run on SMs no GEMM block occupies (pair with
+ * mxg_set_gemm_sm_limit to overlap an exchange with the GEMMs). */
 MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
                                 int64_t n_send, const int32_t* slot_start, const int32_t* dest_base,
-                                int num_slots, int e_local, const uint64_t* peer_bufs,
+                                int num_slots, int e_local, int me, const uint64_t* peer_bufs,
                                 int64_t capacity_rows, int max_blocks, void* stream);
 
-/* Padded local row q -> row back_row[q] of peer_bufs[back_rank[q]] (skipped
- * where back_rank < 0). */
-MXG_API int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* back_rank,
-                              const int32_t* back_row, int64_t m_pad, const uint64_t* peer_bufs,
-                              int world, int64_t capacity_rows, int max_blocks, void* stream);
+/* Padded local rows q = ret_order[i] (i < n_rows) -> row back_row[q] of
+ * peer_bufs[back_rank[q]] (skipped where back_rank < 0). */
+MXG_API int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* ret_order,
+                              int64_t n_rows, const int32_t* back_rank, const int32_t* back_row,
+                              const uint64_t* peer_bufs, int world, int64_t capacity_rows,
+                              int max_blocks, void* stream);
 
 /* Zero the rows q < m_pad of buf with back_rank[q] < 0. */
 MXG_API int mxg_ep_zero_pad_rows(void* buf, int64_t row_bytes, const int32_t* back_rank,
                                  int64_t m_pad, void* stream);
+
+/* Cap on the SMs the grouped GEMMs' persistent grids use (0: all SMs);
+ * process-wide, read at each GEMM launch.  Leaves SMs to kernels that run
+ * concurrently on another stream, such as the peer exchanges above. */
+MXG_API int mxg_set_gemm_sm_limit(int sms);
+MXG_API int mxg_get_gemm_sm_limit(void);
 
 /* ---- byte transpose: dst [cols, rows] = src [rows, cols]^T (uint8) ----------- */
 MXG_API int mxg_transpose_u8(const void* src, int64_t rows, int64_t cols, void* dst, void* stream);

@@ -67,6 +67,9 @@ int* device_error_word() {
 
 int64_t take_injected_stall() { return g_stall_ns.exchange(0); }
 
+static std::atomic<int> g_gemm_sm_limit{0};
+int gemm_sm_limit() { return g_gemm_sm_limit.load(); }
+
 }  // namespace mxg
 
 extern "C" const char* mxg_error_string(int code) {
@@ -101,6 +104,14 @@ extern "C" int mxg_get_device_error(int* code, int clear) {
   }
   return MXG_OK;
 }
+
+extern "C" int mxg_set_gemm_sm_limit(int sms) {
+  if (sms < 0) return MXG_ERR_INVALID_ARGUMENT;
+  mxg::g_gemm_sm_limit.store(sms);
+  return MXG_OK;
+}
+
+extern "C" int mxg_get_gemm_sm_limit(void) { return mxg::g_gemm_sm_limit.load(); }
 
 extern "C" int mxg_debug_inject_stall(int64_t timeout_ns) {
   if (timeout_ns < 0) return MXG_ERR_INVALID_ARGUMENT;

@@ -75,13 +75,33 @@ __global__ void p2p_plan_kernel(const int32_t* __restrict__ C, int world, int E,
 
 // One block per local expert of `me`: for every padded row of its group, the
 // rank and send position the result goes back to (-1 on padding rows).
+// ret_order lists the real rows grouped by home rank in the order me+1,
+// me+2, ..., me (mod world), local experts in order within a rank.
 __global__ void p2p_back_kernel(const int32_t* __restrict__ C, int world, int E, int me, int pad,
                                 const int32_t* __restrict__ pref, const int32_t* __restrict__ gs,
                                 const int32_t* __restrict__ tot, int32_t* __restrict__ back_rank,
-                                int32_t* __restrict__ back_row) {
+                                int32_t* __restrict__ back_row, int32_t* __restrict__ ret_order) {
   const int e_local = E / world;
   const int le = blockIdx.x;
   const int s = me * e_local + le;
+  __shared__ int32_t base_s[MXG_EP_MAX_RANKS];
+  if (threadIdx.x == 0) {
+    // rows from each rank to me, accumulated in the rotated rank order, plus
+    // the rows of that rank in my earlier local experts
+    int32_t run = 0;
+    for (int k = 1; k <= world; ++k) {
+      const int r = (me + k) % world;
+      int32_t before = 0, all = 0;
+      for (int x = 0; x < e_local; ++x) {
+        const int32_t c = C[r * E + me * e_local + x];
+        if (x < le) before += c;
+        all += c;
+      }
+      base_s[r] = run + before;
+      run += all;
+    }
+  }
+  __syncthreads();
   int32_t q0 = gs[s];
   for (int r = 0; r < world; ++r) {
     const int32_t c = C[r * E + s];
@@ -89,6 +109,7 @@ __global__ void p2p_back_kernel(const int32_t* __restrict__ C, int world, int E,
     for (int i = threadIdx.x; i < c; i += blockDim.x) {
       back_rank[q0 + i] = r;
       back_row[q0 + i] = p0 + i;
+      ret_order[base_s[r] + i] = q0 + i;
     }
     q0 += c;
   }
@@ -100,22 +121,50 @@ __global__ void p2p_back_kernel(const int32_t* __restrict__ C, int world, int E,
 }
 
 constexpr int kCopyThreads = 256;
+constexpr int kCopyThreadsExclusive = 1024;
+// Shared memory a copy block claims in exclusive mode (unused): more than an
+// SM running a persistent GEMM block has left, so the copies only land on the
+// SMs the GEMMs were told to leave free.
+constexpr int kExclusiveSmem = 120 * 1024;
 constexpr int kMaxSlotsSmem = MXG_EP_MAX_EXPERTS + 1;
 
+// One warp copies one row, four 16-byte vectors in flight per lane.  Loads
+// and stores are marked streaming (evict-first) so the exchange passes
+// through L2 without displacing the operand tiles of GEMMs running beside it.
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                              int64_t row_vecs, int lane) {
+  int64_t v = lane;
+  for (; v + 96 < row_vecs; v += 128) {
+    const uint4 a = __ldcs(src + v), b = __ldcs(src + v + 32), c = __ldcs(src + v + 64),
+                d = __ldcs(src + v + 96);
+    __stcs(dst + v, a);
+    __stcs(dst + v + 32, b);
+    __stcs(dst + v + 64, c);
+    __stcs(dst + v + 96, d);
+  }
+  for (; v < row_vecs; v += 32) __stcs(dst + v, __ldcs(src + v));
+}
+
 // Dispatch: send position p (slot s, the largest with slot_start[s] <= p)
-// -> row dest_base[s] + p of rank s / e_local.  One warp per row, 16-byte
-// vectors.
-__global__ void __launch_bounds__(kCopyThreads) p2p_dispatch_kernel(
+// -> row dest_base[s] + p of rank s / e_local.  One warp per row.  Send
+// positions are ordered by destination rank; every rank starts with the
+// positions of the rank after it (rotation `rot`), so at any moment the ranks
+// write to different peers instead of all to the same one.
+__global__ void __launch_bounds__(kCopyThreadsExclusive) p2p_dispatch_kernel(
     const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ send_rows,
     int64_t n_send, const int32_t* __restrict__ slot_start, const int32_t* __restrict__ dest_base,
-    int E, int e_local, const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows, int* err) {
+    int E, int e_local, int me, const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows,
+    int* err) {
   __shared__ int32_t ss[kMaxSlotsSmem];
   for (int i = threadIdx.x; i <= E; i += blockDim.x) ss[i] = slot_start[i];
   __syncthreads();
+  const int world = E / e_local;
+  const int64_t rot = ss[((me + 1) % world) * e_local];
   const int lane = threadIdx.x & 31;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n_send;
-       p += warps) {
+  for (int64_t i = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n_send;
+       i += warps) {
+    const int64_t p = (i + rot) % n_send;
     int lo = 0, hi = E - 1;  // last slot with ss[s] <= p
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -126,22 +175,24 @@ __global__ void __launch_bounds__(kCopyThreads) p2p_dispatch_kernel(
       if (lane == 0) atomicCAS(err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
       continue;
     }
-    uint4* dst = reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs;
-    const uint4* s = src + int64_t(send_rows[p]) * row_vecs;
-    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(s + v);
+    warp_copy_row(reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs,
+                  src + int64_t(send_rows[p]) * row_vecs, row_vecs, lane);
   }
   __threadfence_system();
 }
 
-// Combine: padded local row q -> send position back_row[q] of rank back_rank[q].
-__global__ void __launch_bounds__(kCopyThreads) p2p_return_kernel(
-    const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ back_rank,
-    const int32_t* __restrict__ back_row, int64_t m_pad, const uint64_t* __restrict__ peer_bufs,
-    int world, int64_t capacity_rows, int* err) {
+// Combine: padded local row q -> send position back_row[q] of rank
+// back_rank[q], taking the rows in ret_order (grouped by home rank, starting
+// with the rank after this one, as the dispatch does).
+__global__ void __launch_bounds__(kCopyThreadsExclusive) p2p_return_kernel(
+    const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ ret_order,
+    int64_t n_rows, const int32_t* __restrict__ back_rank, const int32_t* __restrict__ back_row,
+    const uint64_t* __restrict__ peer_bufs, int world, int64_t capacity_rows, int* err) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t q = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); q < m_pad;
-       q += warps) {
+  for (int64_t i = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n_rows;
+       i += warps) {
+    const int64_t q = ret_order[i];
     const int r = back_rank[q];
     if (r < 0) continue;
     const int64_t row = back_row[q];
@@ -149,9 +200,8 @@ __global__ void __launch_bounds__(kCopyThreads) p2p_return_kernel(
       if (lane == 0) atomicCAS(err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
       continue;
     }
-    uint4* dst = reinterpret_cast<uint4*>(peer_bufs[r]) + row * row_vecs;
-    const uint4* s = src + q * row_vecs;
-    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(s + v);
+    warp_copy_row(reinterpret_cast<uint4*>(peer_bufs[r]) + row * row_vecs, src + q * row_vecs,
+                  row_vecs, lane);
   }
   __threadfence_system();
 }
@@ -170,11 +220,32 @@ __global__ void __launch_bounds__(kCopyThreads) zero_pad_rows_kernel(uint4* __re
   }
 }
 
-static int copy_grid(int64_t rows, int max_blocks) {
+// Launch shape of a peer-copy kernel.  max_blocks <= 0: as many 256-thread
+// blocks as the rows need (up to 8 per SM), sharing SMs with whatever runs.
+// max_blocks > 0 (exclusive): that many 1024-thread blocks, each claiming
+// kExclusiveSmem so it can only run on an SM no GEMM block occupies.
+struct CopyLaunch {
+  int blocks, threads;
+  size_t smem;
+};
+
+static CopyLaunch copy_launch(int64_t rows, int max_blocks) {
+  if (max_blocks > 0) {
+    const int64_t want = (rows + 31) / 32;
+    return {int(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks))), kCopyThreadsExclusive,
+            size_t(kExclusiveSmem)};
+  }
   const int64_t want = (rows + (kCopyThreads / 32) - 1) / (kCopyThreads / 32);
-  const int64_t cap = max_blocks > 0 ? max_blocks : int64_t(num_sms()) * 8;
-  return int(std::max<int64_t>(1, std::min<int64_t>(want, cap)));
+  return {int(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(num_sms()) * 8))), kCopyThreads, 0};
 }
+
+template <class K>
+static int allow_exclusive_smem(K kernel) {
+  return cuda_status(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kExclusiveSmem + 4096));
+}
+
+static int copy_grid(int64_t rows, int max_blocks) { return copy_launch(rows, max_blocks).blocks; }
 
 }  // namespace mxg
 
@@ -227,14 +298,14 @@ extern "C" size_t mxg_ep_p2p_plan_workspace_size(int world, int num_slots) {
 extern "C" int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slots, int me, int pad,
                                int64_t m_pad, int32_t* slot_start, int32_t* dest_base,
                                int32_t* group_rows, int32_t* group_start, int32_t* back_rank,
-                               int32_t* back_row, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+                               int32_t* back_row, int32_t* ret_order, void* workspace,
+                               size_t workspace_bytes, void* stream) {
   if (!counts_all || !slot_start || !dest_base || !group_rows || !group_start || !workspace)
     return MXG_ERR_INVALID_ARGUMENT;
   if (world < 1 || world > MXG_EP_MAX_RANKS || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
       num_slots % world != 0 || me < 0 || me >= world || pad < 1 || m_pad < 0)
     return MXG_ERR_INVALID_ARGUMENT;
-  if (m_pad > 0 && (!back_rank || !back_row)) return MXG_ERR_INVALID_ARGUMENT;
+  if (m_pad > 0 && (!back_rank || !back_row || !ret_order)) return MXG_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < mxg_ep_p2p_plan_workspace_size(world, num_slots))
     return MXG_ERR_WORKSPACE_TOO_SMALL;
   int st = check_device();
@@ -247,17 +318,18 @@ extern "C" int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slo
                                     slot_start, dest_base, group_rows, group_start);
   if (m_pad > 0)
     p2p_back_kernel<<<num_slots / world, 256, 0, s>>>(counts_all, world, num_slots, me, pad, pref,
-                                                      gs, tot, back_rank, back_row);
+                                                      gs, tot, back_rank, back_row, ret_order);
   return cuda_status(cudaGetLastError());
 }
 
 extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
                                    int64_t n_send, const int32_t* slot_start,
-                                   const int32_t* dest_base, int num_slots, int e_local,
+                                   const int32_t* dest_base, int num_slots, int e_local, int me,
                                    const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
                                    void* stream) {
   if (n_send < 0 || row_bytes < 0 || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
-      e_local < 1 || num_slots % e_local != 0 || capacity_rows < 0)
+      e_local < 1 || num_slots % e_local != 0 || capacity_rows < 0 || me < 0 ||
+      me >= num_slots / e_local)
     return MXG_ERR_INVALID_ARGUMENT;
   if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
   if (n_send == 0 || row_bytes == 0) return MXG_OK;
@@ -267,27 +339,32 @@ extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int
   if (st) return st;
   int* err = device_error_word();
   if (!err) return MXG_ERR_CUDA;
-  p2p_dispatch_kernel<<<copy_grid(n_send, max_blocks), kCopyThreads, 0, (cudaStream_t)stream>>>(
+  const CopyLaunch cl = copy_launch(n_send, max_blocks);
+  if (cl.smem && (st = allow_exclusive_smem(p2p_dispatch_kernel))) return st;
+  p2p_dispatch_kernel<<<cl.blocks, cl.threads, cl.smem, (cudaStream_t)stream>>>(
       reinterpret_cast<const uint4*>(src), row_bytes / 16, send_rows, n_send, slot_start, dest_base,
-      num_slots, e_local, peer_bufs, capacity_rows, err);
+      num_slots, e_local, me, peer_bufs, capacity_rows, err);
   return cuda_status(cudaGetLastError());
 }
 
-extern "C" int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* back_rank,
-                                 const int32_t* back_row, int64_t m_pad, const uint64_t* peer_bufs,
-                                 int world, int64_t capacity_rows, int max_blocks, void* stream) {
-  if (m_pad < 0 || row_bytes < 0 || world < 1 || capacity_rows < 0) return MXG_ERR_INVALID_ARGUMENT;
+extern "C" int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* ret_order,
+                                 int64_t n_rows, const int32_t* back_rank, const int32_t* back_row,
+                                 const uint64_t* peer_bufs, int world, int64_t capacity_rows,
+                                 int max_blocks, void* stream) {
+  if (n_rows < 0 || row_bytes < 0 || world < 1 || capacity_rows < 0) return MXG_ERR_INVALID_ARGUMENT;
   if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
-  if (m_pad == 0 || row_bytes == 0) return MXG_OK;
-  if (!src || !back_rank || !back_row || !peer_bufs) return MXG_ERR_INVALID_ARGUMENT;
+  if (n_rows == 0 || row_bytes == 0) return MXG_OK;
+  if (!src || !ret_order || !back_rank || !back_row || !peer_bufs) return MXG_ERR_INVALID_ARGUMENT;
   if (!aligned16(src)) return MXG_ERR_MISALIGNED;
   int st = check_device();
   if (st) return st;
   int* err = device_error_word();
   if (!err) return MXG_ERR_CUDA;
-  p2p_return_kernel<<<copy_grid(m_pad, max_blocks), kCopyThreads, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint4*>(src), row_bytes / 16, back_rank, back_row, m_pad, peer_bufs,
-      world, capacity_rows, err);
+  const CopyLaunch cl = copy_launch(n_rows, max_blocks);
+  if (cl.smem && (st = allow_exclusive_smem(p2p_return_kernel))) return st;
+  p2p_return_kernel<<<cl.blocks, cl.threads, cl.smem, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint4*>(src), row_bytes / 16, ret_order, n_rows, back_rank, back_row,
+      peer_bufs, world, capacity_rows, err);
   return cuda_status(cudaGetLastError());
 }
 

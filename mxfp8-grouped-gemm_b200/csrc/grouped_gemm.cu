@@ -1010,6 +1010,8 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   int pairs = 0;
   st = configure_kernels(&pairs);
   if (st) return st;
+  const int limit = gemm_sm_limit();  // leave SMs to concurrent kernels (peer exchanges)
+  if (limit > 0) pairs = std::max(1, std::min(pairs, limit / 2));
   uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
   int* meta = reinterpret_cast<int*>(wsb + L.meta_off);
   int* err = device_error_word();

@@ -19,5 +19,7 @@ int num_sms();
 int* device_error_word();
 // Stall-injection limit armed by mxg_debug_inject_stall (consumed by the next launch).
 int64_t take_injected_stall();
+// SMs the persistent GEMMs may use (0: all), set by mxg_set_gemm_sm_limit.
+int gemm_sm_limit();
 
 }  // namespace mxg

@@ -93,7 +93,7 @@ class CudaP2POps:
     def __init__(self):
         self.L = _lib.load()
 
-    def plan(self, counts_all: torch.Tensor, me: int, pad: int, m_pad: int):
+    def plan(self, counts_all: torch.Tensor, me: int, pad: int, m_pad: int, n_recv: int):
         world, E = counts_all.shape
         dev = counts_all.device
         e_local = E // world
@@ -103,30 +103,34 @@ class CudaP2POps:
         group_start = torch.empty(e_local + 1, dtype=torch.int32, device=dev)
         back_rank = torch.empty(max(m_pad, 1), dtype=torch.int32, device=dev)
         back_row = torch.empty(max(m_pad, 1), dtype=torch.int32, device=dev)
+        ret_order = torch.empty(max(m_pad, 1), dtype=torch.int32, device=dev)
         ws = _lib.workspace(self.L.mxg_ep_p2p_plan_workspace_size(world, E), dev)
         _lib.check(self.L.mxg_ep_p2p_plan(counts_all.contiguous().data_ptr(), world, E, me, pad, m_pad,
                                           slot_start.data_ptr(), dest_base.data_ptr(),
                                           group_rows.data_ptr(), group_start.data_ptr(),
-                                          back_rank.data_ptr(), back_row.data_ptr(), ws.data_ptr(),
-                                          ws.numel(), _lib.stream_ptr(dev)), "mxg_ep_p2p_plan")
-        return slot_start, dest_base, group_rows, group_start, back_rank[:m_pad], back_row[:m_pad]
+                                          back_rank.data_ptr(), back_row.data_ptr(),
+                                          ret_order.data_ptr(), ws.data_ptr(), ws.numel(),
+                                          _lib.stream_ptr(dev)), "mxg_ep_p2p_plan")
+        return (slot_start, dest_base, group_rows, group_start, back_rank[:m_pad], back_row[:m_pad],
+                ret_order[:n_recv])
 
-    def dispatch(self, src, send_rows, slot_start, dest_base, e_local, peer_ptrs, capacity_rows,
+    def dispatch(self, src, send_rows, slot_start, dest_base, e_local, me, peer_ptrs, capacity_rows,
                  max_blocks=0):
         src = src.contiguous()
         row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
         _lib.check(self.L.mxg_ep_dispatch_p2p(src.data_ptr() if src.numel() else None, row_bytes,
                                               send_rows.data_ptr(), send_rows.numel(),
                                               slot_start.data_ptr(), dest_base.data_ptr(),
-                                              dest_base.numel(), e_local, peer_ptrs.data_ptr(),
+                                              dest_base.numel(), e_local, me, peer_ptrs.data_ptr(),
                                               capacity_rows, max_blocks,
                                               _lib.stream_ptr(src.device)), "mxg_ep_dispatch_p2p")
 
-    def ret(self, src, back_rank, back_row, peer_ptrs, capacity_rows, max_blocks=0):
+    def ret(self, src, ret_order, back_rank, back_row, peer_ptrs, capacity_rows, max_blocks=0):
         src = src.contiguous()
         row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
         _lib.check(self.L.mxg_ep_return_p2p(src.data_ptr() if src.numel() else None, row_bytes,
-                                            back_rank.data_ptr(), back_row.data_ptr(), back_rank.numel(),
+                                            ret_order.data_ptr(), ret_order.numel(),
+                                            back_rank.data_ptr(), back_row.data_ptr(),
                                             peer_ptrs.data_ptr(), peer_ptrs.numel(), capacity_rows,
                                             max_blocks, _lib.stream_ptr(src.device)),
                    "mxg_ep_return_p2p")
@@ -262,6 +266,7 @@ class DispatchPlan:
     dest_base: torch.Tensor | None = None    # [E] destination row of position p = dest_base[s] + p
     back_rank: torch.Tensor | None = None    # [M_pad] home rank of each padded row (-1: padding)
     back_row: torch.Tensor | None = None     # [M_pad] send position on that rank
+    ret_order: torch.Tensor | None = None    # [n_recv] real rows grouped by home rank, rotated
 
 
 class ExpertParallel:
@@ -394,12 +399,13 @@ class ExpertParallel:
                 self._ensure_buffer(name, max(worst, need), row_bytes, x.device)
         if self.capacity.get("ret", (0, 0))[0] < int(sent.max()):
             self._ensure_buffer("ret", max(n_cap * k, int(sent.max())), row_bytes, x.device)
-        slot_start, dest_base, group_rows, _, back_rank, back_row = self.p2p.plan(C, self.rank, pad, m_pad)
+        slot_start, dest_base, group_rows, _, back_rank, back_row, ret_order = self.p2p.plan(
+            C, self.rank, pad, m_pad, recv_rows)
         send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
         recv_splits = Ch[:, self.rank * El:(self.rank + 1) * El].sum(1).tolist()
         plan = DispatchPlan(send_rows, slot_pos, send_splits, recv_splits, None, None,
                             group_rows, padded[self.rank].tolist(), recv_rows, n, k,
-                            slot_start, dest_base, back_rank, back_row)
+                            slot_start, dest_base, back_rank, back_row, ret_order)
         return self.dispatch_like(x, plan, "x"), plan
 
     def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy") -> torch.Tensor:
@@ -415,7 +421,7 @@ class ExpertParallel:
             local = buf.view(m_pad, x)
             self.p2p.zero_pad_rows(local, plan.back_rank)
             self.p2p.dispatch(x, plan.send_rows, plan.slot_start, plan.dest_base, self.e_local,
-                              buf.ptrs, rows, self.p2p_max_blocks)
+                              self.rank, buf.ptrs, rows, self.p2p_max_blocks)
             self._barrier(x.device)
             return local
         send_buf = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
@@ -425,13 +431,22 @@ class ExpertParallel:
     def combine(self, y_local: torch.Tensor, plan: DispatchPlan, weights=None) -> torch.Tensor:
         """y_local [M_pad, H'] results in the dispatch layout -> [n, H'] =
         sum over each token's choices (weighted when weights [n, k] given)."""
+        return self.combine_finish(self.combine_send(y_local, plan), plan, weights)
+
+    def combine_send(self, y_local: torch.Tensor, plan: DispatchPlan) -> torch.Tensor:
+        """First half of ``combine``: every result row back to its home rank.
+        Returns this rank's rows in send order [n*k, H'] (with the p2p
+        transport: a view of the "ret" buffer, valid until the next combine)."""
         if plan.back_rank is not None:
             buf = self.buffers["ret"]
             rows, row_bytes = self.capacity["ret"]
-            self.p2p.ret(y_local, plan.back_rank, plan.back_row, buf.ptrs, rows, self.p2p_max_blocks)
+            self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
+                         self.p2p_max_blocks)
             self._barrier(y_local.device)
-            ret = buf.view(plan.n_tokens * plan.topk, y_local)
-            return self.ops.combine(ret, plan.slot_pos, weights, plan.n_tokens, plan.topk)
+            return buf.view(plan.n_tokens * plan.topk, y_local)
         back_buf = self.ops.gather(y_local, plan.back, plan.recv_rows)
-        ret = self._a2a(back_buf, plan.n_tokens * plan.topk, plan.send_splits, plan.recv_splits)
+        return self._a2a(back_buf, plan.n_tokens * plan.topk, plan.send_splits, plan.recv_splits)
+
+    def combine_finish(self, ret: torch.Tensor, plan: DispatchPlan, weights=None) -> torch.Tensor:
+        """Second half of ``combine``: the weighted sum over each token's choices."""
         return self.ops.combine(ret, plan.slot_pos, weights, plan.n_tokens, plan.topk)

@@ -35,7 +35,10 @@ class ExpertFFN:
     [E_local, H, I] bf16 (quantised here once)."""
 
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                 comm_stream: torch.cuda.Stream | None = None):
+                 comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0):
+        """With a comm stream, the dy dispatch and the combine's return run
+        beside the GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM
+        blocks while they do, and runs the peer copies only there."""
         self.ep = ep
         E, I2, H = w_gate_up.shape
         E2, H2, I = w_down.shape
@@ -51,6 +54,13 @@ class ExpertFFN:
         self.wdt = (q.view(E, I, H), s.view(E, I, H // 32))
         del wdt
         self.comm = comm_stream
+        self.reserve = reserve_sms if comm_stream is not None else 0
+        if self.reserve:
+            self.ep.p2p_max_blocks = self.reserve
+            sms = torch.cuda.get_device_properties(w_gate_up.device).multi_processor_count
+            self.gemm_sms = sms - self.reserve
+        else:
+            self.gemm_sms = 0
         self.marks = None           # optional list of (name, cuda event) for profiling
 
     def _mark(self, name):
@@ -88,7 +98,8 @@ class ExpertFFN:
             dy_ready.record()
         xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
         self._mark("quantize_x")
-        gu = self._fwd((xq, xs), self.wgu, offs)
+        with ops.gemm_sm_limit(self.gemm_sms):             # beside the dy exchange
+            gu = self._fwd((xq, xs), self.wgu, offs)
         self._mark("fwd_gate_up")
         hq, hs, ia_d, ias_d = ops.swiglu_quantize(gu)        # h is never written in bf16
         self._mark("swiglu_quantize_h")
@@ -97,13 +108,14 @@ class ExpertFFN:
         if comm is not None:
             comm.wait_stream(main)
         with side():
-            out = ep.combine(y_local, plan, probs)
+            ret = ep.combine_send(y_local, plan)
         main.wait_event(dy_ready)
         dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
         self._mark("quantize_dy")
-        dh = self._fwd((dyq, dys), self.wdt, offs)
-        self._mark("dgrad_down")
-        dw_d = self._wgrad((go_d, gos_d), (ia_d, ias_d), offs)
+        with ops.gemm_sm_limit(self.gemm_sms):             # beside the combine's return
+            dh = self._fwd((dyq, dys), self.wdt, offs)
+            self._mark("dgrad_down")
+            dw_d = self._wgrad((go_d, gos_d), (ia_d, ias_d), offs)
         self._mark("wgrad_down")
         _, _, go_g, gos_g = ops.swiglu_bwd_quantize(gu, dh)  # dgu is never written in bf16
         self._mark("quantize_gate_up")
@@ -114,6 +126,7 @@ class ExpertFFN:
             # this wait (the next dispatch syncs on main before the comm
             # stream waits on main), so no record_stream is needed.
             main.wait_stream(comm)
+        out = ep.combine_finish(ret, plan, probs)
         self._mark("combine")
         return out, dw_gu, dw_d, plan
 

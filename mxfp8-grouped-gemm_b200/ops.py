@@ -260,6 +260,23 @@ def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
     return dgu
 
 
+class gemm_sm_limit:
+    """Context manager: the grouped GEMMs launched inside use at most ``sms``
+    SMs (None or 0: all), leaving the rest to kernels on other streams."""
+
+    def __init__(self, sms):
+        self.sms = int(sms or 0)
+
+    def __enter__(self):
+        L = _lib.load()
+        self.prev = L.mxg_get_gemm_sm_limit()
+        _lib.check(L.mxg_set_gemm_sm_limit(self.sms), "mxg_set_gemm_sm_limit")
+        return self
+
+    def __exit__(self, *exc):
+        _lib.load().mxg_set_gemm_sm_limit(self.prev)
+
+
 # ---------------------------------------------------------------- two-phase plans
 class GroupedFwdPlan:
     """Groups and packed scales of one grouped forward, prepared once in a

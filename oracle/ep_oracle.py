@@ -132,7 +132,9 @@ def p2p_plan(counts_all: np.ndarray, me: int, pad: int = 32):
     slot counts C [world, E]: the owners' receive buffers use the regroup
     layout above, so send position p of slot s lands on rank s // E_local at
     row dest_base[s] + p, and padded row q of ``me`` returns to
-    (back_rank[q], back_row[q])."""
+    (back_rank[q], back_row[q]); ret_order lists the real rows by home rank,
+    starting with rank me+1 (so that the ranks send to different peers at the
+    same time)."""
     C = np.asarray(counts_all, dtype=np.int64)
     W, E = C.shape
     El = E // W
@@ -158,6 +160,8 @@ def p2p_plan(counts_all: np.ndarray, me: int, pad: int = 32):
             back_rank[q:q + c] = r
             back_row[q:q + c] = pref[r, s] + np.arange(c)
             q += c
+    # real rows grouped by home rank, ranks in the order me+1, me+2, ... (mod W)
+    ret_order = [q for kk in range(1, W + 1) for q in range(m_pad) if back_rank[q] == (me + kk) % W]
     i32 = lambda a: np.asarray(a, dtype=np.int32)
     return (i32(pref[me]), i32(dest_base), i32(group_rows), i32(group_start), i32(back_rank),
-            i32(back_row))
+            i32(back_row), i32(ret_order))

@@ -156,7 +156,8 @@ def test_p2p_plan_places_rows_like_regroup(world):
             bufs[s // (E // world)][dest_base[s] + p] = xs[r][sr[p]]
     for d in range(world):
         assert np.array_equal(bufs[d], out[d][0])
-        _, _, gr, gst, brank, brow = ep_oracle.p2p_plan(C, d)
+        _, _, gr, gst, brank, brow, order = ep_oracle.p2p_plan(C, d)
+        assert sorted(order.tolist()) == [q for q in range(brank.size) if brank[q] >= 0]
         assert np.array_equal(gr, out[d][2]["group_rows"])
         for q in range(brank.size):
             if brank[q] >= 0:

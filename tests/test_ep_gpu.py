@@ -163,14 +163,14 @@ def test_p2p_kernels_emulated_ranks(mxg, cuda_dev, world, k, H):
     plans = []
     for r in range(world):
         m_pad = out[r][0].shape[0]
-        pl = p2p.plan(C, r, 32, m_pad)
+        pl = p2p.plan(C, r, 32, m_pad, int(out[r][1].sum()))
         want = ep_oracle.p2p_plan(C.cpu().numpy(), r)
         for got, w in zip(pl, want):
             assert np.array_equal(got.cpu().numpy(), w)
         plans.append(pl)
         p2p.zero_pad_rows(bufs[r][:m_pad], pl[4])
     for r in range(world):
-        p2p.dispatch(xs[r], routed[r][1], plans[r][0], plans[r][1], E // world, ptrs, cap)
+        p2p.dispatch(xs[r], routed[r][1], plans[r][0], plans[r][1], E // world, r, ptrs, cap)
     for d in range(world):
         m_pad = out[d][0].shape[0]
         assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), out[d][0])
@@ -181,7 +181,7 @@ def test_p2p_kernels_emulated_ranks(mxg, cuda_dev, world, k, H):
     rptrs = torch.tensor([t.data_ptr() for t in rets], dtype=torch.int64, device=cuda_dev)
     for d in range(world):
         m_pad = out[d][0].shape[0]
-        p2p.ret(bufs[d][:m_pad], plans[d][4], plans[d][5], rptrs, ret_rows)
+        p2p.ret(bufs[d][:m_pad], plans[d][6], plans[d][4], plans[d][5], rptrs, ret_rows)
     for r in range(world):
         if ns[r] == 0:
             continue
@@ -198,11 +198,11 @@ def test_p2p_dispatch_rejects_rows_past_capacity(mxg, cuda_dev):
     ep, p2p = mxg.ep.CudaEpOps(), mxg.ep.CudaP2POps()
     c, sr, sp = ep.route(torch.from_numpy(ids).to(cuda_dev), E)
     C = c.view(1, E)
-    pl = p2p.plan(C, 0, 32, int(((c.cpu().numpy() + 31) // 32 * 32).sum()))
+    pl = p2p.plan(C, 0, 32, int(((c.cpu().numpy() + 31) // 32 * 32).sum()), int(c.sum()))
     small = torch.zeros(8, H, dtype=torch.bfloat16, device=cuda_dev)
     guard = torch.zeros(64, H, dtype=torch.bfloat16, device=cuda_dev)
     ptrs = torch.tensor([small.data_ptr()], dtype=torch.int64, device=cuda_dev)
-    p2p.dispatch(_bf16(x, cuda_dev), sr, pl[0], pl[1], E, ptrs, 8)
+    p2p.dispatch(_bf16(x, cuda_dev), sr, pl[0], pl[1], E, 0, ptrs, 8)
     assert mxg.device_error() == mxg._lib.MXG_ERR_WORKSPACE_TOO_SMALL
     assert torch.all(guard == 0)
 
