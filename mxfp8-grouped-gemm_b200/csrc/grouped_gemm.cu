@@ -256,7 +256,101 @@ struct PackArgs {
   int k_fwd;
 };
 
+// One block per (group, operand row block): thread r owns row r of the block
+// and walks that row's scales across the group's contraction range (one
+// contiguous run of bytes per thread), writing its word of every chunk.
+// A side: 2*mbp blocks of 128 rows per group; B side: one block per N tile
+// (<= 240 rows, two 128-row halves).
 __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
+  __shared__ int ustart[MXG_MAX_GROUPS + 1];  // B side: first unit of each group
+  MetaView mv{const_cast<int*>(p.meta), p.E};
+  const int mbp = ceil_div(p.n_out, 2 * kBM);
+  if (p.side == 1) {
+    for (int i = threadIdx.x; i <= p.E; i += blockDim.x) ustart[i] = mv.tile_start()[i] / mbp;
+    __syncthreads();
+  }
+  const int units = p.side == 0 ? p.E * 2 * mbp : ustart[p.E];
+  const int r = threadIdx.x;
+  const int rows_per_unit = p.side == 0 ? kBM : 2 * kBM;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    int e, blk;
+    if (p.side == 0) {
+      e = u / (2 * mbp);
+      blk = u - e * 2 * mbp;
+    } else {
+      int lo = 0, hi = p.E - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (ustart[mid] <= u) lo = mid; else hi = mid - 1;
+      }
+      e = lo;
+      blk = u - ustart[e];
+    }
+    const int kbn = mv.g_kb()[e];
+    const int gstart = mv.g_start()[e], glen = mv.g_len()[e];
+    int row0, valid, col0, col_end, chunk0;
+    if (p.side == 0) {
+      row0 = (p.mode == MODE_FWD ? e * p.n_out : 0) + blk * kBM;
+      valid = min(kBM, p.n_out - blk * kBM);
+      chunk0 = mv.g_asf()[e] + blk * kbn;
+    } else {
+      const int ext = p.mode == MODE_FWD ? glen : p.n_ext;
+      int n0, nlen;
+      split_rows(ext, mv.g_nt()[e], blk, n0, nlen);
+      row0 = (p.mode == MODE_FWD ? gstart : 0) + n0;
+      valid = nlen;
+      chunk0 = mv.g_bsf()[e] + blk * kbn;
+    }
+    if (p.mode == MODE_FWD) {
+      col0 = 0;
+      col_end = p.k_fwd / 32;
+    } else {
+      col0 = gstart / 32;
+      col_end = (gstart + glen) / 32;
+    }
+    if (r >= rows_per_unit) continue;
+    const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
+    const int half = r >> 7, rr = r & 127;
+    uint8_t* d0 = p.dst + int64_t(chunk0) * chunk_bytes + half * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
+    const bool live = p.src && r < valid;
+    const uint8_t* srow = live ? p.src + int64_t(row0 + r) * p.src_ld : p.src;
+    // the row's bytes [col0, col_end) as 4-byte words: aligned loads, joined
+    // with a funnel shift when the run does not start on a word boundary
+    // (reads stay inside the tensor: the aligned-down start is at or after
+    // its 16-byte-aligned base, and a word is only used if it ends in the row)
+    const uint8_t* row_end = srow + p.src_ld;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(srow + col0);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = uint32_t(a & 3u) * 8u;
+#pragma unroll 4
+    for (int kb = 0; kb < kbn; ++kb) {
+      const int col = col0 + kb * 4;
+      uint32_t word = 0x7F7F7F7Fu;
+      if (live) {
+        if (col + 4 <= col_end && sh == 0) {
+          word = __ldg(wp + kb);
+        } else if (col + 4 <= col_end &&
+                   reinterpret_cast<const uint8_t*>(wp + kb + 2) <= row_end) {
+          word = __funnelshift_r(__ldg(wp + kb), __ldg(wp + kb + 1), sh);
+        } else {
+          word = 0;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t v = col + kk < col_end ? uint32_t(__ldg(srow + col + kk)) : 0x7Fu;
+            word |= v << (8 * kk);
+          }
+        }
+      }
+      *reinterpret_cast<uint32_t*>(d0 + int64_t(kb) * chunk_bytes) = word;
+    }
+  }
+}
+
+
+// Chunk-parallel variant: one block per chunk at a time, thread r reads the
+// four bytes of row r.  Faster than the row walk when the scale rows are not
+// word aligned (the wgrad's token-contiguous scales, M/32 bytes per row).
+__global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
   __shared__ int base_s[MXG_MAX_GROUPS + 1];
   MetaView mv{const_cast<int*>(p.meta), p.E};
   const int* base = p.side == 0 ? mv.g_asf() : mv.g_bsf();
@@ -991,12 +1085,21 @@ static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
   const int sms = num_sms();
   PackArgs pa{meta, P.E, P.mode, 0, reinterpret_cast<const uint8_t*>(a_sc), P.kc / 32,
               wsb + L.sfa_off, int(P.n_out), int(P.n_ext), int(P.kc)};
-  pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pa);
+  // A side: E * 2 * mbp units of 128 rows; B side: one unit per N tile (the
+  // count is only known on the device: grid-stride over a generous grid)
+  const int mbp = int((P.n_out + 2 * kBM - 1) / (2 * kBM));
+  const int a_units = P.E * 2 * mbp;
   PackArgs pb = pa;
   pb.side = 1;
   pb.src = reinterpret_cast<const uint8_t*>(b_sc);
   pb.dst = wsb + L.sfb_off;
-  pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+  if (P.mode == MODE_FWD) {  // K/32-byte scale rows: word-aligned row walks
+    pack_scales_kernel<<<std::max(1, std::min(a_units, sms * 16)), 128, 0, stream>>>(pa);
+    pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+  } else {
+    pack_scales_chunk_kernel<<<sms * 8, 128, 0, stream>>>(pa);
+    pack_scales_chunk_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+  }
   return cuda_status(cudaGetLastError());
 }
 
