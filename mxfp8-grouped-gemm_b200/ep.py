@@ -191,10 +191,14 @@ class PeerBuffer:
             n *= d
         return self.local[:n].view(like.dtype).view(shape)
 
-    def close(self):
+    def close_peers(self):
+        """Unmap the other ranks' buffers."""
         for p in self.opened:
             self.L.mxg_peer_close(ctypes.c_void_p(p))
         self.opened = []
+
+    def free(self):
+        """Free this rank's buffer (after every rank has unmapped it)."""
         if self.own:
             self.local = None
             self.L.mxg_peer_free(ctypes.c_void_p(self.own))
@@ -308,12 +312,17 @@ class ExpertParallel:
         self._flag = None
 
     def close(self):
-        """Release the peer buffers (collective: every rank calls it)."""
+        """Release the peer buffers (collective: every rank calls it).  Every
+        rank unmaps the others' buffers before any rank frees its own."""
         if self.buffers:
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
             for b in self.buffers.values():
-                b.close()
+                b.close_peers()
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            for b in self.buffers.values():
+                b.free()
             self.buffers, self.capacity = {}, {}
 
     def _barrier(self, device):
@@ -332,7 +341,9 @@ class ExpertParallel:
         if old is not None:
             torch.cuda.synchronize()
             dist.barrier(group=self.group)
-            old.close()
+            old.close_peers()
+            dist.barrier(group=self.group)
+            old.free()
         self.buffers[name] = PeerBuffer(max(rows, 1) * row_bytes, self.group, self.world, self.rank, device)
         self.capacity[name] = (max(rows, 1), row_bytes)
 
@@ -395,9 +406,11 @@ class ExpertParallel:
         worst = W * n_cap * min(k, El) + El * (pad - 1)
         need = max(int(m_pad_all.max()), 1)
         for name in ("x", "dy"):
-            if self.capacity.get(name, (0, 0))[0] < need:
+            rows, rb = self.capacity.get(name, (0, 0))
+            if rows < need or rb != row_bytes:
                 self._ensure_buffer(name, max(worst, need), row_bytes, x.device)
-        if self.capacity.get("ret", (0, 0))[0] < int(sent.max()):
+        rows, rb = self.capacity.get("ret", (0, 0))
+        if rows < int(sent.max()) or rb != row_bytes:
             self._ensure_buffer("ret", max(n_cap * k, int(sent.max())), row_bytes, x.device)
         slot_start, dest_base, group_rows, _, back_rank, back_row, ret_order = self.p2p.plan(
             C, self.rank, pad, m_pad, recv_rows)
@@ -440,6 +453,8 @@ class ExpertParallel:
         if plan.back_rank is not None:
             buf = self.buffers["ret"]
             rows, row_bytes = self.capacity["ret"]
+            if y_local.shape[0] and y_local.element_size() * y_local[0].numel() != row_bytes:
+                raise ValueError("combine rows must have the dispatched rows' size")
             self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
                          self.p2p_max_blocks)
             self._barrier(y_local.device)
