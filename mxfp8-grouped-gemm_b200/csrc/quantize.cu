@@ -296,46 +296,48 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
   }
   if (a.qt == nullptr) return;
   __syncthreads();
-  // column pass: thread t encodes tile columns 2p, 2p+1 (p = t % CW) over the
-  // 32 rows of row block t / CW; the row blocks of a column write adjacent
-  // 32-byte runs of the transposed output
-  const int pcol = t % CW, rblk = t / CW;
-  if (r0 + 32 * rblk >= a.rows) return;
-  int64_t col0;
-  if (KIND == DUAL_SWIGLU_GRAD) {
-    const int64_t j = c0 + 2 * (pcol % (CW / 2));
-    if (j >= a.inter) return;
-    col0 = pcol < CW / 2 ? j : a.inter + j;
-  } else {
-    col0 = c0 + 2 * pcol;
-    if (col0 >= a.cols) return;
-  }
-  // two passes over shared memory (amax, then encode) keep few registers live
-  const uint32_t* colp = &tile[32 * rblk][pcol];
-  uint32_t m0 = 0, m1 = 0;
+  // Column pass.  Work item = (column pair p, 32-row block rb, half h): the
+  // two lanes of a pair (h = lane & 1) take rows [32rb, 32rb+16) and
+  // [32rb+16, 32rb+32) of columns 2p, 2p+1, share the block amax with one
+  // shuffle, and store their 16 bytes of each column side by side, so one
+  // store instruction writes whole 32-byte sectors of the transposed output.
+  constexpr int kItems = CW * (R / 32) * 2;
+#pragma unroll 1
+  for (int it = t; it < kItems; it += 256) {
+    const int h = it & 1, pcol = (it >> 1) % CW, rblk = (it >> 1) / CW;
+    const bool row_ok = r0 + 32 * rblk < a.rows;
+    int64_t col0;
+    bool col_ok;
+    if (KIND == DUAL_SWIGLU_GRAD) {
+      const int64_t j = c0 + 2 * (pcol % (CW / 2));
+      col_ok = j < a.inter;
+      col0 = pcol < CW / 2 ? j : a.inter + j;
+    } else {
+      col0 = c0 + 2 * pcol;
+      col_ok = col0 < a.cols;
+    }
+    // (the partner lane always has the same rblk and pcol: same predicate)
+    const uint32_t* colp = &tile[32 * rblk + 16 * h][pcol];
+    uint32_t w[16];
+    uint32_t m0 = 0, m1 = 0;
 #pragma unroll
-  for (int r = 0; r < 32; ++r) {
-    const uint32_t wr = colp[r * CW];
-    m0 = max(m0, wr & 0x7FFFu);
-    m1 = max(m1, (wr >> 16) & 0x7FFFu);
-  }
-  const uint32_t b0 = rceil_byte(m0), b1 = rceil_byte(m1);
-  const float f0 = descale_of(b0), f1 = descale_of(b1);
-  const int64_t rb = r0 + 32 * rblk;
-  uint4* d0 = reinterpret_cast<uint4*>(a.qt + col0 * a.rows + rb);
-  uint4* d1 = reinterpret_cast<uint4*>(a.qt + (col0 + 1) * a.rows + rb);
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {  // rows [16hh, 16hh + 16): one 16-byte store per column
+    for (int r = 0; r < 16; ++r) {
+      w[r] = colp[r * CW];
+      m0 = max(m0, w[r] & 0x7FFFu);
+      m1 = max(m1, (w[r] >> 16) & 0x7FFFu);
+    }
+    m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+    m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+    if (!row_ok || !col_ok) continue;
+    const uint32_t b0 = rceil_byte(m0), b1 = rceil_byte(m1);
+    const float f0 = descale_of(b0), f1 = descale_of(b1);
     uint32_t o0[4], o1[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t w4[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) w4[q] = colp[(16 * hh + 4 * j + q) * CW];
-      const uint32_t a01 = cvt_e4m3x2(bf16_lo(w4[0]) * f0, bf16_lo(w4[1]) * f0);
-      const uint32_t a23 = cvt_e4m3x2(bf16_lo(w4[2]) * f0, bf16_lo(w4[3]) * f0);
-      const uint32_t b01 = cvt_e4m3x2(bf16_hi(w4[0]) * f1, bf16_hi(w4[1]) * f1);
-      const uint32_t b23 = cvt_e4m3x2(bf16_hi(w4[2]) * f1, bf16_hi(w4[3]) * f1);
+      const uint32_t a01 = cvt_e4m3x2(bf16_lo(w[4 * j]) * f0, bf16_lo(w[4 * j + 1]) * f0);
+      const uint32_t a23 = cvt_e4m3x2(bf16_lo(w[4 * j + 2]) * f0, bf16_lo(w[4 * j + 3]) * f0);
+      const uint32_t b01 = cvt_e4m3x2(bf16_hi(w[4 * j]) * f1, bf16_hi(w[4 * j + 1]) * f1);
+      const uint32_t b23 = cvt_e4m3x2(bf16_hi(w[4 * j + 2]) * f1, bf16_hi(w[4 * j + 3]) * f1);
       o0[j] = a01 | (a23 << 16);
       o1[j] = b01 | (b23 << 16);
       if (b0 == 255u || b1 == 255u) {
@@ -343,8 +345,8 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t x0 = (o0[j] >> (8 * q)) & 0xFFu, x1 = (o1[j] >> (8 * q)) & 0xFFu;
-          if (b0 == 255u) x0 = fix_nan_byte(x0, w4[q] & 0xFFFFu);
-          if (b1 == 255u) x1 = fix_nan_byte(x1, w4[q] >> 16);
+          if (b0 == 255u) x0 = fix_nan_byte(x0, w[4 * j + q] & 0xFFFFu);
+          if (b1 == 255u) x1 = fix_nan_byte(x1, w[4 * j + q] >> 16);
           p0 |= x0 << (8 * q);
           p1 |= x1 << (8 * q);
         }
@@ -352,11 +354,15 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
         o1[j] = p1;
       }
     }
-    __stcs(d0 + hh, make_uint4(o0[0], o0[1], o0[2], o0[3]));
-    __stcs(d1 + hh, make_uint4(o1[0], o1[1], o1[2], o1[3]));
+    const int64_t rb = r0 + 32 * rblk;
+    *reinterpret_cast<uint4*>(a.qt + col0 * a.rows + rb + 16 * h) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+    *reinterpret_cast<uint4*>(a.qt + (col0 + 1) * a.rows + rb + 16 * h) =
+        make_uint4(o1[0], o1[1], o1[2], o1[3]);
+    if (h == 0) {
+      a.st[col0 * (a.rows / 32) + rb / 32] = uint8_t(b0);
+      a.st[(col0 + 1) * (a.rows / 32) + rb / 32] = uint8_t(b1);
+    }
   }
-  a.st[col0 * (a.rows / 32) + rb / 32] = uint8_t(b0);
-  a.st[(col0 + 1) * (a.rows / 32) + rb / 32] = uint8_t(b1);
 }
 
 template <int KIND>
@@ -428,6 +434,11 @@ extern "C" int mxg_quantize_colwise(const void* x_bf16, int64_t rows, int64_t co
   if (!aligned16(x_bf16) || !aligned16(qt_e4m3)) return MXG_ERR_MISALIGNED;
   if (rows == 0 || cols == 0) return MXG_OK;
   if (rows / 32 > 65535) return MXG_ERR_BAD_SHAPE;
+  if (cols % 32 == 0) {  // the tiled kernel writes whole 32-byte sectors of qt: faster
+    DualArgs a{reinterpret_cast<const uint4*>(x_bf16), nullptr, rows, cols, 0, nullptr, nullptr,
+               reinterpret_cast<uint8_t*>(qt_e4m3), reinterpret_cast<uint8_t*>(scales_t_e8m0)};
+    return launch_dual<DUAL_PLAIN>(a, stream);
+  }
   int st = check_device();
   if (st) return st;
   dim3 grid(unsigned((cols + kColPerBlock - 1) / kColPerBlock), unsigned(rows / 32));
