@@ -261,6 +261,24 @@ struct PackArgs {
 // contiguous run of bytes per thread), writing its word of every chunk.
 // A side: 2*mbp blocks of 128 rows per group; B side: one block per N tile
 // (<= 240 rows, two 128-row halves).
+// Bytes [col, col + 4) of a scale row as one word (0x7F past col_end): an
+// aligned load, two joined with a funnel shift when the run is not word
+// aligned (used only if the second word still ends inside the row), or byte
+// loads at the edges.
+__device__ __forceinline__ uint32_t scale_word(const uint8_t* srow, const uint32_t* wp, uint32_t sh,
+                                               const uint8_t* row_end, int kb, int col, int col_end) {
+  if (col + 4 <= col_end && sh == 0) return __ldg(wp + kb);
+  if (col + 4 <= col_end && reinterpret_cast<const uint8_t*>(wp + kb + 2) <= row_end)
+    return __funnelshift_r(__ldg(wp + kb), __ldg(wp + kb + 1), sh);
+  uint32_t word = 0;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint32_t v = col + kk < col_end ? uint32_t(__ldg(srow + col + kk)) : 0x7Fu;
+    word |= v << (8 * kk);
+  }
+  return word;
+}
+
 __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
   __shared__ int ustart[MXG_MAX_GROUPS + 1];  // B side: first unit of each group
   MetaView mv{const_cast<int*>(p.meta), p.E};
@@ -270,9 +288,16 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
     __syncthreads();
   }
   const int units = p.side == 0 ? p.E * 2 * mbp : ustart[p.E];
-  const int r = threadIdx.x;
+  // A thread packs rows q, q+32, q+64, q+96 of one 128-row half and stores
+  // their four words as one 16-byte vector (a warp writes a whole 512-byte
+  // chunk half per k-block instead of scattering 4-byte words).
   const int rows_per_unit = p.side == 0 ? kBM : 2 * kBM;
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+  const int tpu = rows_per_unit / 4;            // threads per unit
+  const int upb = int(blockDim.x) / tpu;        // units per block at a time
+  const int sub = int(threadIdx.x) / tpu, t = int(threadIdx.x) % tpu;
+  const int half = t >> 5, q = t & 31;
+  const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
+  for (int u = blockIdx.x * upb + sub; u < units; u += gridDim.x * upb) {
     int e, blk;
     if (p.side == 0) {
       e = u / (2 * mbp);
@@ -308,40 +333,30 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
       col0 = gstart / 32;
       col_end = (gstart + glen) / 32;
     }
-    if (r >= rows_per_unit) continue;
-    const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
-    const int half = r >> 7, rr = r & 127;
-    uint8_t* d0 = p.dst + int64_t(chunk0) * chunk_bytes + half * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
-    const bool live = p.src && r < valid;
-    const uint8_t* srow = live ? p.src + int64_t(row0 + r) * p.src_ld : p.src;
-    // the row's bytes [col0, col_end) as 4-byte words: aligned loads, joined
-    // with a funnel shift when the run does not start on a word boundary
-    // (reads stay inside the tensor: the aligned-down start is at or after
-    // its 16-byte-aligned base, and a word is only used if it ends in the row)
-    const uint8_t* row_end = srow + p.src_ld;
-    const uintptr_t a = reinterpret_cast<uintptr_t>(srow + col0);
-    const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    const uint32_t sh = uint32_t(a & 3u) * 8u;
-#pragma unroll 4
+    // per row j: start of its run, the aligned word pointer and the shift
+    const uint8_t* srow[4];
+    const uint32_t* wp[4];
+    uint32_t sh[4];
+    bool live[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = half * kBM + q + 32 * j;
+      live[j] = p.src && r < valid;
+      srow[j] = live[j] ? p.src + int64_t(row0 + r) * p.src_ld : p.src;
+      const uintptr_t a = reinterpret_cast<uintptr_t>(srow[j] + col0);
+      wp[j] = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+      sh[j] = uint32_t(a & 3u) * 8u;
+    }
+    uint4* d = reinterpret_cast<uint4*>(p.dst + int64_t(chunk0) * chunk_bytes + half * 512 + q * 16);
+#pragma unroll 2
     for (int kb = 0; kb < kbn; ++kb) {
       const int col = col0 + kb * 4;
-      uint32_t word = 0x7F7F7F7Fu;
-      if (live) {
-        if (col + 4 <= col_end && sh == 0) {
-          word = __ldg(wp + kb);
-        } else if (col + 4 <= col_end &&
-                   reinterpret_cast<const uint8_t*>(wp + kb + 2) <= row_end) {
-          word = __funnelshift_r(__ldg(wp + kb), __ldg(wp + kb + 1), sh);
-        } else {
-          word = 0;
+      uint32_t w[4];
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t v = col + kk < col_end ? uint32_t(__ldg(srow + col + kk)) : 0x7Fu;
-            word |= v << (8 * kk);
-          }
-        }
-      }
-      *reinterpret_cast<uint32_t*>(d0 + int64_t(kb) * chunk_bytes) = word;
+      for (int j = 0; j < 4; ++j)
+        w[j] = live[j] ? scale_word(srow[j], wp[j], sh[j], srow[j] + p.src_ld, kb, col, col_end)
+                       : 0x7F7F7F7Fu;
+      d[int64_t(kb) * (chunk_bytes / 16)] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
@@ -356,11 +371,15 @@ __global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
   const int* base = p.side == 0 ? mv.g_asf() : mv.g_bsf();
   for (int i = threadIdx.x; i <= p.E; i += blockDim.x) base_s[i] = base[i];
   __syncthreads();
-  const int total = base_s[p.E];
-  const int chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
-  const int rows_per_chunk = p.side == 0 ? 128 : 256;
-  const int r = threadIdx.x;
-  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+  // one warp per 128-row half of a chunk: lane q packs rows q, q+32, q+64,
+  // q+96 into one 16-byte store
+  const int halves = p.side == 0 ? 1 : 2;
+  const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
+  const int total = base_s[p.E] * halves;
+  const int lane = threadIdx.x & 31;
+  const int warps = int(gridDim.x * blockDim.x) >> 5;
+  for (int item = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < total; item += warps) {
+    const int c = item / halves, half = item - c * halves;
     int lo = 0, hi = p.E - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -389,7 +408,10 @@ __global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
       col0 = gstart / 32 + kb * 4;
       col_end = (gstart + glen) / 32;
     }
-    if (r < rows_per_chunk) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = half * kBM + lane + 32 * j;
       uint32_t word = 0x7F7F7F7Fu;
       if (p.src && r < valid) {
         const uint8_t* srow = p.src + int64_t(row0 + r) * p.src_ld;
@@ -397,14 +419,14 @@ __global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const int col = col0 + kk;
-          const uint32_t v = col < col_end ? uint32_t(srow[col]) : 0x7Fu;
+          const uint32_t v = col < col_end ? uint32_t(__ldg(srow + col)) : 0x7Fu;
           word |= v << (8 * kk);
         }
       }
-      const int half = r >> 7, rr = r & 127;
-      uint8_t* d = p.dst + int64_t(c) * chunk_bytes + half * 512 + (rr & 31) * 16 + (rr >> 5) * 4;
-      *reinterpret_cast<uint32_t*>(d) = word;
+      w[j] = word;
     }
+    *reinterpret_cast<uint4*>(p.dst + int64_t(c) * chunk_bytes + half * 512 + lane * 16) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -1094,8 +1116,9 @@ static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
   pb.src = reinterpret_cast<const uint8_t*>(b_sc);
   pb.dst = wsb + L.sfb_off;
   if (P.mode == MODE_FWD) {  // K/32-byte scale rows: word-aligned row walks
-    pack_scales_kernel<<<std::max(1, std::min(a_units, sms * 16)), 128, 0, stream>>>(pa);
-    pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+    // 128 threads = four 128-row A units or two 256-row B units at a time
+    pack_scales_kernel<<<std::max(1, std::min((a_units + 3) / 4, sms * 16)), 128, 0, stream>>>(pa);
+    pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pb);
   } else {
     pack_scales_chunk_kernel<<<sms * 8, 128, 0, stream>>>(pa);
     pack_scales_chunk_kernel<<<sms * 8, 256, 0, stream>>>(pb);
