@@ -5,7 +5,8 @@ directory name is not a Python identifier) after putting the repository root
 on ``sys.path``.  The compute runs in ``libmxg.so`` (C ABI, ``include/mxg.h``);
 build it with ``python mxfp8-grouped-gemm_b200/build.py``.
 """
-from . import _lib, ep, moe, ops, workloads
+from . import _lib, autograd, ep, moe, ops, workloads
+from .autograd import grouped_mm
 from .ep import ExpertParallel
 from ._lib import MxgError, device_error, raise_device_error
 from .fused_fwd import fused_grouped_fwd, reference_grouped_gemm
@@ -17,5 +18,6 @@ __all__ = [
     "fused_grouped_fwd", "reference_grouped_gemm", "fwd_ge",
     "wgrad_fused", "wgrad_prepare", "wgrad_kernel",
     "quantize_rowwise", "quantize_colwise", "to_mxfp8_dim0", "to_mxfp8_dim1",
-    "ExpertParallel", "MxgError", "device_error", "raise_device_error", "ep", "moe", "ops", "workloads",
+    "grouped_mm", "ExpertParallel", "MxgError", "device_error", "raise_device_error",
+    "autograd", "ep", "moe", "ops", "workloads",
 ]
