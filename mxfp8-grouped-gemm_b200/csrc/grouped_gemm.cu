@@ -878,6 +878,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
           issue_store(&tmOut, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e, true);
           slot ^= 1u;
+        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && cols_here == 16) {
+          // bf16 remainder of a 240-column tile: row = lane, 16 columns (32 B),
+          // unswizzled rows (the store's box); the tensor edge clips it
+          slot_ready();
+          uint8_t* buf = epi + slot * 2048;
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            *reinterpret_cast<uint4*>(buf + lane * 32 + u * 16) = make_uint4(
+                pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
+                pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
+          issue_store(&tmOut16, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e, true);
+          slot ^= 1u;
         } else {
           store_chunk<MODE>(g, ti, row, c0, v, false);
         }
@@ -996,6 +1010,20 @@ static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t r
                    base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
+}
+
+// dW [E, rows, cols] bf16, box {16 cols (32 B), 32 rows, 1}, no swizzle.
+static int make_out_tmap_wgrad16(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols) {
+  auto enc = get_encode_fn();
+  if (!enc) return MXG_ERR_CUDA;
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(E)};
+  cuuint64_t strides[2] = {cuuint64_t(cols) * 2, cuuint64_t(cols) * 2 * cuuint64_t(rows)};
+  cuuint32_t box[3] = {16, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
@@ -1158,6 +1186,10 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   if (wgrad_tma) {
     st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype);
     if (st) return st;
+    if (out_dtype == MXG_DTYPE_BF16) {  // 16-column remainders of bf16 tiles
+      st = make_out_tmap_wgrad16(&tmOut16, out, P.E, P.n_out, P.n_ext);
+      if (st) return st;
+    }
   }
   // TMA stores need the output row stride (N elements) to be a multiple of 16 bytes
   const bool fwd_tma = P.mode == MODE_FWD && (P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2)) % 16 == 0;
