@@ -393,10 +393,15 @@ def sample_experts(wl, n=2):
 
 # ---------------------------------------------------------------- EP layer (config 5)
 EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
-# our kernels per layer step: route 3, dispatch gathers 2+1, dy dispatch 2,
-# fused quantisations 4 (x, swiglu, dy, swiglu backward), grouped fwd 3 x 5,
-# wgrad 2 x 4, combine gather + combine 2
-EP_LAUNCHES_PER_STEP = 3 + 3 + 2 + 4 + 15 + 8 + 2
+# our kernels per layer step (NCCL's own kernels not counted): fused
+# quantisations 4 (x, swiglu, dy, swiglu backward), grouped fwd 3 x 5,
+# wgrad 2 x 4, plus the exchange:
+#   p2p:  route 3, plan 2, zero pad + peer dispatch 2, dy zero pad + peer
+#         dispatch 2, peer return 1, combine 1
+#   nccl: route 3, send gather + regroup + gather 3, dy gathers 2, return
+#         gather 1, combine 1
+EP_LAUNCHES_PER_STEP = {"p2p": 4 + 15 + 8 + 3 + 2 + 2 + 2 + 1 + 1,
+                        "nccl": 4 + 15 + 8 + 3 + 3 + 2 + 1 + 1}
 
 
 class EpLayerBench:
@@ -568,7 +573,7 @@ def run_ep_mxg(args, rank, world, local):
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
                "padded_rows_this_rank", "segments_ms_rank0", "gemm_tflops_rank0")},
            "cpu_baseline": None, "e2e": e2e,
-           "gpu_launches": args.steps * EP_LAUNCHES_PER_STEP, "clocks": clk.summary()}
+           "gpu_launches": args.steps * EP_LAUNCHES_PER_STEP[r["transport"]], "clocks": clk.summary()}
     if rank == 0:
         print(json.dumps(out), flush=True)
 
