@@ -297,11 +297,59 @@ def time_steps(calls, steps, warmup, world):
     return total_ms / steps, {k: v / steps for k, v in run_ms.items()}, {k: v / steps for k, v in prep_ms.items()}
 
 
+def pipelined_e2e(host_inputs, compute, host_outputs, steps):
+    """Host buffers end to end, the copies pipelined against the compute:
+    step i+1's inputs go up on an H2D stream while step i computes, and step
+    i's results come down on a D2H stream while step i+1 computes (PCIe is
+    full duplex).  Two device input sets alternate.  Returns ms per step from
+    the first upload to the last download (events on the main stream's
+    timeline)."""
+    main = torch.cuda.current_stream()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    sets = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host_inputs.items()}
+            for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        with torch.cuda.stream(up):
+            for k, v in host_inputs.items():
+                sets[i % 2][k].copy_(v, non_blocking=True)
+            ready[i % 2].record()
+
+    def run(n):
+        up.wait_stream(main)
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                if i >= 1:
+                    up.wait_event(free[(i + 1) % 2])   # step i-1 is done with that set
+                upload(i + 1)
+            main.wait_event(ready[i % 2])
+            outs = compute(sets[i % 2])
+            free[i % 2].record(main)
+            down.wait_stream(main)
+            with torch.cuda.stream(down):
+                for h, o in zip(host_outputs, outs):
+                    h.copy_(o, non_blocking=True)
+                    o.record_stream(down)
+        main.wait_stream(down)
+
+    run(2)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(main)
+    run(steps)
+    e.record(main)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
 def e2e_measure(wl, steps):
     """Host-buffer end to end through the public API: pinned host operands ->
     H2D -> fused_grouped_fwd / wgrad_fused -> D2H of the results."""
     m = pkg()
-    dev = wl.y.device
     host = {}
     for name in ("xq", "xs", "wq", "ws", "offs", "go_d", "gos_d", "ia_d", "ias_d", "go_g", "gos_g",
                  "ia_g", "ias_g", "sizes"):
@@ -315,24 +363,13 @@ def e2e_measure(wl, steps):
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in (y_h, dwd_h, dwg_h))
 
-    def step():
-        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+    def compute(d):
         y = m.fused_grouped_fwd(d["xq"], d["wq"], d["offs"], d["xs"], d["ws"])
         dwd = m.wgrad_fused(d["go_d"], d["ia_d"], d["sizes"], d["gos_d"], d["ias_d"], out_dtype=torch.float32)
         dwg = m.wgrad_fused(d["go_g"], d["ia_g"], d["sizes"], d["gos_g"], d["ias_g"], out_dtype=torch.float32)
-        y_h.copy_(y, non_blocking=True)
-        dwd_h.copy_(dwd, non_blocking=True)
-        dwg_h.copy_(dwg, non_blocking=True)
+        return y, dwd, dwg
 
-    step()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
+    ms = pipelined_e2e(host, compute, [y_h, dwd_h, dwg_h], steps)
     return ms, h2d, d2h
 
 
@@ -470,8 +507,8 @@ def time_ep_layer(lb, steps, warmup, world):
 
 def e2e_ep_layer(lb, steps):
     """Through the public API with host buffers: pinned x, dy, expert ids and
-    router probs -> H2D -> layer step -> D2H of the combined output."""
-    dev = lb.x.device
+    router probs -> H2D -> layer step -> D2H of the combined output, the
+    copies pipelined against the compute (pipelined_e2e)."""
     host = {k: torch.empty(getattr(lb, k).shape, dtype=getattr(lb, k).dtype, pin_memory=True)
             for k in ("x", "ids", "probs", "dy")}
     for k, h in host.items():
@@ -480,20 +517,11 @@ def e2e_ep_layer(lb, steps):
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = out_h.numel() * out_h.element_size()
 
-    def step():
-        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+    def compute(d):
         out, _, _, _ = lb.step(d["x"], d["ids"], d["probs"], d["dy"])
-        out_h.copy_(out, non_blocking=True)
+        return (out,)
 
-    step()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    return s.elapsed_time(e) / steps, h2d, d2h
+    return pipelined_e2e(host, compute, [out_h], steps), h2d, d2h
 
 
 def sum_over_ranks(v, world):
