@@ -228,6 +228,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
   constexpr int R = kTileRows, CW = kTileCols / 2;      // tile rows, tile width in bf16x2 words
   constexpr int CPR = kTileCols / 8;                     // 16-byte chunks per tile row
   __shared__ __align__(16) uint32_t tile[R][CW];
+  __shared__ __align__(4) uint8_t col_scales[kTileCols][R / 32];  // column pass -> one write per column
   const int64_t r0 = int64_t(blockIdx.y) * R;
   const int t = threadIdx.x;
   // tile columns -> tensor columns: contiguous, except for the gradient where
@@ -359,8 +360,31 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
     *reinterpret_cast<uint4*>(a.qt + (col0 + 1) * a.rows + rb + 16 * h) =
         make_uint4(o1[0], o1[1], o1[2], o1[3]);
     if (h == 0) {
-      a.st[col0 * (a.rows / 32) + rb / 32] = uint8_t(b0);
-      a.st[(col0 + 1) * (a.rows / 32) + rb / 32] = uint8_t(b1);
+      col_scales[2 * pcol][rblk] = uint8_t(b0);
+      col_scales[2 * pcol + 1][rblk] = uint8_t(b1);
+    }
+  }
+  // The tile's column scales leave together: one thread per column writes
+  // its R/32 consecutive bytes (one word when aligned) instead of single
+  // bytes that each cost a 32-byte sector on the way to L2.
+  __syncthreads();
+  if (t < kTileCols) {
+    int64_t gcol;
+    if (KIND == DUAL_SWIGLU_GRAD) {
+      const int64_t j = c0 + (t % (kTileCols / 2));
+      if (j >= a.inter) return;
+      gcol = t < kTileCols / 2 ? j : a.inter + j;
+    } else {
+      gcol = c0 + t;
+      if (gcol >= a.cols) return;
+    }
+    const int64_t rem = (a.rows - r0) / 32;
+    const int nb = int(rem < R / 32 ? rem : R / 32);
+    uint8_t* dst = a.st + gcol * (a.rows / 32) + r0 / 32;
+    if (R / 32 == 4 && nb == 4 && (reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
+      *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(col_scales[t]);
+    } else {
+      for (int b = 0; b < nb; ++b) dst[b] = col_scales[t][b];
     }
   }
 }
