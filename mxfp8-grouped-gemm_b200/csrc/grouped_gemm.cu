@@ -728,36 +728,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * kAccStride;
         const uint32_t n_mma = uint32_t(ti.nlen + 15) & ~15u;
         const uint32_t idesc0 = make_idesc_mxf8(2 * kBM, n_mma);
-        for (int kb = 0; kb < ti.kb_count; ++kb) {
-          if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.full[stage]), phase, wc))) {
+        // k-steps go in pairs: both stages' scale factors are copied to TMEM
+        // before the pair's MMAs, so the tensor pipe switches between copies
+        // and MMAs once per two k-steps (a copy issued between MMAs costs
+        // far more than its own duration; one pair group measured ~4% fewer
+        // cycles than a copy group per k-step)
+        for (int kb = 0; kb < ti.kb_count; kb += 2) {
+          const bool two = kb + 1 < ti.kb_count;
+          const uint32_t stage2 = stage + 1 == kStages ? 0u : stage + 1;
+          const uint32_t phase2 = stage + 1 == kStages ? phase ^ 1u : phase;
+          bool ready = mbar_wait(smem_u32(&s.full[stage]), phase, wc);
+          if (ready && two) ready = mbar_wait(smem_u32(&s.full[stage2]), phase2, wc);
+          if (!__all_sync(0xffffffffu, ready)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sfa_t = tmem_base + (sf_buf ? kSfCol1 : kSfCol0);
-          sf_buf ^= 1u;
-          const uint32_t sfb_t = sfa_t + kSfbOff;
-          const uint32_t sfa_s = smem_u32(s.sfa[stage]), sfb_s = smem_u32(s.sfb[stage]);
-          const int rem = ti.klen - kb * kBK;
-          const int nk = rem >= kBK ? 4 : rem / 32;
-          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(s.a[stage]));
-          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(s.b[stage]));
-          if (elect_one_sync()) {
-            tc_cp_32x128b_warpx4_pair(sfa_t, sdesc_sf_chunk(sfa_s));
-            tc_cp_32x128b_warpx4_pair(sfb_t, sdesc_sf_chunk(sfb_s));
-            tc_cp_32x128b_warpx4_pair(sfb_t + 4, sdesc_sf_chunk(sfb_s + 512));
+          auto step = [&](uint32_t stg, uint32_t buf, int kbi) {
+            const uint32_t sfa_t = tmem_base + (buf ? kSfCol1 : kSfCol0);
+            const uint32_t sfb_t = sfa_t + kSfbOff;
+            const int rem = ti.klen - kbi * kBK;
+            const int nk = rem >= kBK ? 4 : rem / 32;
+            const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(s.a[stg]));
+            const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(s.b[stg]));
             for (int kk = 0; kk < nk; ++kk) {
               tc_mma_mxf8_pair(d_tmem, adesc + uint64_t(2 * kk), bdesc + uint64_t(2 * kk),
                                idesc_with_sf_id(idesc0, kk, kk), sfa_t | (uint32_t(kk) << 30),
-                               sfb_t | (uint32_t(kk) << 30), (kb | kk) != 0 ? 1u : 0u);
+                               sfb_t | (uint32_t(kk) << 30), (kbi | kk) != 0 ? 1u : 0u);
             }
-            tc_commit_pair_mc(smem_u32(&s.empty[stage]), 0x3);
+            tc_commit_pair_mc(smem_u32(&s.empty[stg]), 0x3);
+          };
+          auto copy_sf = [&](uint32_t stg, uint32_t buf) {
+            const uint32_t sfa_t = tmem_base + (buf ? kSfCol1 : kSfCol0);
+            const uint32_t sfb_t = sfa_t + kSfbOff;
+            const uint32_t sfa_s = smem_u32(s.sfa[stg]), sfb_s = smem_u32(s.sfb[stg]);
+            tc_cp_32x128b_warpx4_pair(sfa_t, sdesc_sf_chunk(sfa_s));
+            tc_cp_32x128b_warpx4_pair(sfb_t, sdesc_sf_chunk(sfb_s));
+            tc_cp_32x128b_warpx4_pair(sfb_t + 4, sdesc_sf_chunk(sfb_s + 512));
+          };
+          if (elect_one_sync()) {
+            copy_sf(stage, sf_buf);
+            if (two) copy_sf(stage2, sf_buf ^ 1u);
+            step(stage, sf_buf, kb);
+            if (two) step(stage2, sf_buf ^ 1u, kb + 1);
           }
           __syncwarp();
           issued = true;
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+          if (!two) sf_buf ^= 1u;
+          const int adv = two ? 2 : 1;
+          for (int i = 0; i < adv; ++i) {
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
         if (!ok) break;
@@ -847,23 +870,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             slot ^= 1u;
           }
         } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && f32) {
-          // row = lane, 16 fp32 columns (64 B) per store, 64-byte swizzle; the
-          // store clips at the tensor edge, and a half past this tile's
-          // columns is skipped
+          // row = lane; 32 fp32 columns (128 B rows, 128-byte swizzle) per
+          // store from the warp's whole 4 KiB buffer, or 16 (64 B rows,
+          // 64-byte swizzle) for the remainder of a 240-column tile; the
+          // store clips at the tensor edge.  Half as many store requests as
+          // 64-byte rows through two 2 KiB slots, which measured slower.
           const int r0 = ti.mb * kBM + warp * 32;
+          if (epi_pending) {
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+          if (cols_here == 32) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (c0 + 16 * h < ti.nlen) {
-              slot_ready();
-              uint8_t* buf = epi + slot * 2048;
+            for (int u = 0; u < 8; ++u)
+              *reinterpret_cast<uint4*>(epi + lane * 128 + ((u ^ (lane & 7)) * 16)) =
+                  make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            issue_store(&tmOut, smem_u32(epi), ti.n0 + c0, r0, ti.e, true);
+          } else {
 #pragma unroll
-              for (int u = 0; u < 4; ++u)
-                *reinterpret_cast<uint4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) =
-                    make_uint4(v[16 * h + 4 * u], v[16 * h + 4 * u + 1], v[16 * h + 4 * u + 2],
-                               v[16 * h + 4 * u + 3]);
-              issue_store(&tmOut, smem_u32(buf), ti.n0 + c0 + 16 * h, r0, ti.e, true);
-              slot ^= 1u;
-            }
+            for (int u = 0; u < 4; ++u)
+              *reinterpret_cast<uint4*>(epi + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) =
+                  make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+            issue_store(&tmOut16, smem_u32(epi), ti.n0 + c0, r0, ti.e, true);
           }
         } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && cols_here == 32) {
           // bf16: row = lane, 32 columns (64 B), 64-byte swizzle
@@ -994,22 +1022,23 @@ static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, 
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
-// dW [E, rows, cols] output, box {64 bytes of columns (16 fp32 or 32 bf16),
-// 32 rows, 1}, 64-byte swizzle (the epilogue's staging layout).
+// dW [E, rows, cols] output, box {row_bytes of columns (64: 16 fp32 or 32
+// bf16; 128: 32 fp32), 32 rows, 1}, swizzle of the same width (the
+// epilogue's staging layout).
 static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols,
-                               int out_dtype) {
+                               int out_dtype, int row_bytes) {
   auto enc = get_encode_fn();
   if (!enc) return MXG_ERR_CUDA;
   const bool f32 = out_dtype == MXG_DTYPE_F32;
   const cuuint64_t esz = f32 ? 4 : 2;
   cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(E)};
   cuuint64_t strides[2] = {cuuint64_t(cols) * esz, cuuint64_t(cols) * esz * cuuint64_t(rows)};
-  cuuint32_t box[3] = {cuuint32_t(64 / esz), 32, 1};
+  cuuint32_t box[3] = {cuuint32_t(row_bytes / int(esz)), 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                    base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MXG_OK : MXG_ERR_CUDA;
 }
 
@@ -1184,9 +1213,14 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   // TMA stores need the output row stride to be a multiple of 16 bytes
   const bool wgrad_tma = P.mode == MODE_WGRAD && (P.n_ext * out_esz) % 16 == 0;
   if (wgrad_tma) {
-    st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype);
-    if (st) return st;
-    if (out_dtype == MXG_DTYPE_BF16) {  // 16-column remainders of bf16 tiles
+    if (out_dtype == MXG_DTYPE_F32) {  // 32-column stores, 16-column remainders
+      st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype, 128);
+      if (st) return st;
+      st = make_out_tmap_wgrad(&tmOut16, out, P.E, P.n_out, P.n_ext, out_dtype, 64);
+      if (st) return st;
+    } else {  // 32-column stores, 16-column remainders of bf16 tiles
+      st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype, 64);
+      if (st) return st;
       st = make_out_tmap_wgrad16(&tmOut16, out, P.E, P.n_out, P.n_ext);
       if (st) return st;
     }
