@@ -446,7 +446,7 @@ class EpLayerBench:
     gradients and its local experts."""
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
-                 transport="auto", p2p_blocks=0, reserve_sms=0):
+                 transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16"):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -468,7 +468,9 @@ class EpLayerBench:
         w_gu = torch.randn(e_loc, GATE_UP, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
         w_d = torch.randn(e_loc, HIDDEN, INTER, generator=g, device=dev, dtype=torch.bfloat16) * 0.02
         self.comm = torch.cuda.Stream() if (overlap and world > 1) else None
+        self.wgrad_dtype = wgrad_dtype
         self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm,
+                                     wgrad_dtype=torch.float32 if wgrad_dtype == "fp32" else torch.bfloat16,
                                      reserve_sms=reserve_sms)
         del w_gu, w_d
         torch.cuda.synchronize()
@@ -575,7 +577,8 @@ def run_ep_mxg(args, rank, world, local):
     """The N>1 bench line: config 5 across the process group."""
     pkg()._lib.load()
     lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
-                      transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms)
+                      transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
+                      wgrad_dtype=args.ep_wgrad_dtype)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -595,6 +598,8 @@ def run_ep_mxg(args, rank, world, local):
                       "hidden": HIDDEN, "intermediate": INTER, "placement": r["placement"],
                       "comm_overlap": r["overlap"], "transport": r["transport"],
                       "reserved_sms": r["reserve_sms"],
+                      "dw_dtype": lb.wgrad_dtype + (" (the reference's wgrad output dtype)"
+                                                    if lb.wgrad_dtype == "bf16" else ""),
                       "parallelism": f"ep{world}",
                       "l2": "operands > L2 (no flush needed)"},
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
@@ -698,13 +703,15 @@ def run_mxg(args, rank, world, local):
     if not args.no_ep and args.case == "dsv3":
         del wl, calls
         torch.cuda.empty_cache()
-        lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=False)
+        lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=False,
+                          wgrad_dtype=args.ep_wgrad_dtype)
         r = measure_ep_layer(lb, world, min(args.steps, 50), args.warmup)
         del lb
         out["ep_layer_1gpu"] = {"value": round(r["value"], 2), "unit": "TFLOPS",
                                 "ms_per_step": round(r["ms_per_step"], 4),
                                 "note": "config 5 layer on one GPU (all 256 experts, 16384 tokens): "
                                         "the same per-GPU work as each rank of the N>1 lines",
+                                "dw_dtype": args.ep_wgrad_dtype,
                                 "gemm_tflops": r["gemm_tflops_rank0"],
                                 "segments_ms": r["segments_ms_rank0"],
                                 "recv_rows": r["recv_rows_per_rank"]["max"]}
@@ -855,6 +862,9 @@ def main():
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
                     help="EP layer token exchange: NVLink peer stores or NCCL all_to_all")
     ap.add_argument("--p2p-blocks", type=int, default=0, help="grid cap of the peer-store kernels (0: default)")
+    ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
+                    help="weight-gradient dtype of the config-5 expert layer (bf16: the reference's "
+                         "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
     ap.add_argument("--reserve-sms", type=int, default=0,
                     help="EP layer with --overlap: SMs kept free of GEMM blocks for the peer copies")
     args = ap.parse_args()

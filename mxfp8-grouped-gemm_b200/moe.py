@@ -35,10 +35,16 @@ class ExpertFFN:
     [E_local, H, I] bf16 (quantised here once)."""
 
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
-                 comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0):
+                 comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
+                 wgrad_dtype: torch.dtype = torch.bfloat16):
         """With a comm stream, the dy dispatch and the combine's return run
         beside the GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM
-        blocks while they do, and runs the peer copies only there."""
+        blocks while they do, and runs the peer copies only there.
+        wgrad_dtype is the weight gradients' dtype: bf16 by default, as the
+        reference's wgrad returns them (``wgrad_fused.py:41``), or fp32."""
+        if wgrad_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
+        self.wgrad_dtype = wgrad_dtype
         self.ep = ep
         E, I2, H = w_gate_up.shape
         E2, H2, I = w_down.shape
@@ -75,13 +81,15 @@ class ExpertFFN:
         return ops.grouped_fwd(q, wq, offs, s, ws, out_dtype=out_dtype, offs_kind=_lib.OFFS_SIZES)
 
     def _wgrad(self, go, ia, offs):
-        return ops.grouped_wgrad(go[0], ia[0], offs, go[1], ia[1], out_dtype=torch.float32,
+        return ops.grouped_wgrad(go[0], ia[0], offs, go[1], ia[1], out_dtype=self.wgrad_dtype,
                                  offs_kind=_lib.OFFS_SIZES, num_groups=self.E)
 
     def step(self, x, expert_ids, probs, dy):
         """Forward and weight gradients of one layer step.  x, dy [n, H] bf16,
         expert_ids [n, k] int32, probs [n, k] fp32.  Returns (out [n, H] bf16,
-        dW_gate_up [E_local, 2I, H] fp32, dW_down [E_local, H, I] fp32, plan)."""
+        dW_gate_up [E_local, 2I, H], dW_down [E_local, H, I] (wgrad_dtype), plan).
+        dy is the gradient of each routed row's expert output: it is sent to
+        every expert the token chose, unweighted."""
         ep = self.ep
         main = torch.cuda.current_stream()
         comm = self.comm

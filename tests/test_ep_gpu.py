@@ -1,8 +1,10 @@
 """Expert-parallel routing kernels vs the oracle (bit-exact for the integer
 maps and row moves; the weighted combine within one bf16 ulp of the oracle's
 fp32 sum; swiglu within 1e-2 relative of a torch fp32 reference), one expert
-layer through dispatch -> MXFP8 GEMMs -> combine against fp64, and a
-world-size-2 NCCL dispatch/combine when the box has two GPUs."""
+layer through dispatch -> MXFP8 GEMMs -> combine against fp64, the whole
+moe.ExpertFFN step (forward and both weight gradients) against a host
+restatement, and a world-size-2 NCCL dispatch/combine when the box has two
+GPUs."""
 import multiprocessing as mp
 import os
 
@@ -12,6 +14,7 @@ import torch
 
 from ep_support import free_port, make_rank_inputs
 from oracle import ep_oracle
+from oracle import mxfp8_oracle as orc_mod
 
 pytestmark = pytest.mark.gpu
 
@@ -288,3 +291,78 @@ def test_swiglu_bwd_matches_autograd(mxg, cuda_dev, R, I):
     ref = ref_in.grad
     err = ((dgu.float() - ref).norm() / ref.norm().clamp_min(1e-30)).item()
     assert err <= 1e-2
+
+
+def _ffn_emulation(x, dy, wgu, wd, ids, p, E):
+    """The layer step of moe.ExpertFFN restated on the host: per expert, MXFP8
+    (oracle quantiser) operands, fp64 products, bf16 GEMM outputs, SiLU-gated
+    product and its gradient in fp64; also the unquantised fp64 result."""
+    n, k = ids.shape
+    H, I = x.shape[1], wd.shape[2]
+    bf = lambda a: orc_mod.bf16_bits_to_f32(orc_mod.f32_to_bf16_bits(a.astype(np.float32))).astype(np.float64)
+    q_row = lambda a: orc_mod.dequantize(*orc_mod.quantize_rowwise(orc_mod.f32_to_bf16_bits(a.astype(np.float32))))
+    q_col = lambda a: orc_mod.dequantize(*orc_mod.quantize_colwise(orc_mod.f32_to_bf16_bits(a.astype(np.float32))))
+    sig = lambda g: 1.0 / (1.0 + np.exp(-g))
+    res = {}
+    for quant in (True, False):
+        out = np.zeros((n, H))
+        dwgu = np.zeros((E, 2 * I, H))
+        dwd = np.zeros((E, H, I))
+        for e in range(E):
+            rows = [(t, j) for t in range(n) for j in range(k) if ids[t, j] == e]
+            if not rows:
+                continue
+            T = np.array([t for t, _ in rows])
+            pad = (-len(T)) % 32
+            xe = np.concatenate([x[T], np.zeros((pad, H))])
+            dye = np.concatenate([dy[T], np.zeros((pad, H))])
+            if quant:
+                gu = bf(q_row(xe) @ q_row(wgu[e]).T)
+            else:
+                gu = xe @ wgu[e].T
+            g, u = gu[:, :I], gu[:, I:]
+            h = g * sig(g) * u
+            y = bf(q_row(h) @ q_row(wd[e]).T) if quant else h @ wd[e].T
+            dh = bf(q_row(dye) @ q_row(np.ascontiguousarray(wd[e].T)).T) if quant else dye @ wd[e]
+            s_ = sig(g)
+            dgu = np.concatenate([dh * u * s_ * (1 + g * (1 - s_)), dh * g * s_], 1)
+            if quant:
+                dwd[e] = q_col(dye) @ q_col(h).T
+                dwgu[e] = q_col(dgu) @ q_col(xe).T
+            else:
+                dwd[e] = dye.T @ h
+                dwgu[e] = dgu.T @ xe
+            for r, (t, j) in enumerate(rows):
+                out[t] += p[t, j] * y[r]
+        res[quant] = (out, dwgu, dwd)
+    return res
+
+
+@pytest.mark.parametrize("wgrad_dtype", [torch.bfloat16, torch.float32])
+def test_expert_ffn_world1(mxg, cuda_dev, wgrad_dtype):
+    """moe.ExpertFFN on one rank: the combined output and both weight
+    gradients against a host restatement of the same MXFP8 layer step
+    (relative Frobenius <= 3e-2: the fused SwiGLU quantisers round their fp32
+    inputs once, the restatement through bf16) and against the unquantised
+    fp64 layer (<= 0.12; MXFP8 alone costs ~0.066 here)."""
+    E, H, I, n, k = 8, 256, 128, 300, 2
+    rng = np.random.default_rng(3)
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)
+    x, dy = bf(rng.standard_normal((n, H))), bf(rng.standard_normal((n, H)) * 1e-2)
+    wgu, wd = bf(rng.standard_normal((E, 2 * I, H)) * 0.05), bf(rng.standard_normal((E, H, I)) * 0.05)
+    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(n)]).astype(np.int32)
+    p = rng.random((n, k)) + 0.1
+    p = (p / p.sum(1, keepdims=True)).astype(np.float32)
+    layer = mxg.moe.ExpertFFN(mxg.ExpertParallel(E), wgu.to(cuda_dev), wd.to(cuda_dev),
+                              wgrad_dtype=wgrad_dtype)
+    out, dw_gu, dw_d, plan = layer.step(x.to(cuda_dev), torch.from_numpy(ids).to(cuda_dev),
+                                        torch.from_numpy(p).to(cuda_dev), dy.to(cuda_dev))
+    assert mxg.device_error() == 0
+    assert dw_gu.dtype == wgrad_dtype and dw_d.dtype == wgrad_dtype
+    ref = _ffn_emulation(x.float().numpy().astype(np.float64), dy.float().numpy().astype(np.float64),
+                         wgu.float().numpy().astype(np.float64), wd.float().numpy().astype(np.float64),
+                         ids, p.astype(np.float64), E)
+    got = [t.float().cpu().numpy().astype(np.float64) for t in (out, dw_gu, dw_d)]
+    for name, g, rq, rf in zip(("out", "dw_gate_up", "dw_down"), got, ref[True], ref[False]):
+        eq, ef = orc_mod.rel_frobenius(g, rq), orc_mod.rel_frobenius(g, rf)
+        assert eq <= 3e-2 and ef <= 0.12, (name, eq, ef)
