@@ -260,6 +260,119 @@ class Workload:
 
 LAUNCHES_PER_CALL = {"fwd_gate_up": 5, "wgrad_down": 4, "wgrad_gate_up": 4}  # our kernels per API call
 
+# config 3 (Mixtral-shaped, few large groups): 8 experts, hidden 4096, FFN 14336
+MIX_E, MIX_HIDDEN, MIX_FFN, MIX_TOKENS, MIX_TOPK = 8, 4096, 14336, 32768, 2
+
+
+class MixtralWorkload:
+    """Device-resident MXFP8 operands of config 3: gate/up (N=28672, K=4096)
+    and down (N=4096, K=14336) projections, forward and weight gradients."""
+
+    def __init__(self, seed=0, device="cuda"):
+        m = pkg()
+        W = m.workloads
+        self.split = sp = W.topk_softmax_split(MIX_TOKENS, MIX_E, MIX_TOPK, seed=seed)
+        self.M = sp.M
+        dev = torch.device(device)
+        E, H, F = MIX_E, MIX_HIDDEN, MIX_FFN
+        self.offs = torch.from_numpy(sp.offs_cumulative()).to(dev)
+        self.sizes = torch.from_numpy(sp.padded.astype(np.int32)).to(dev)
+        t = {}
+
+        def q_rows(name, bf):
+            t[name] = m.quantize_rowwise(bf)
+
+        def q_cols(name, bf):
+            t[name] = m.quantize_colwise(bf)
+
+        x = W.routed_activations(sp, H, 1.0, dev, seed + 20)
+        q_rows("x", x)
+        q_cols("x_t", x)
+        del x
+        h = W.routed_activations(sp, F, 1.0, dev, seed + 21)
+        q_rows("h", h)
+        q_cols("h_t", h)
+        del h
+        dy = W.routed_activations(sp, 2 * F, 1e-2, dev, seed + 22)
+        q_cols("dgu_t", dy)
+        del dy
+        dy = W.routed_activations(sp, H, 1e-2, dev, seed + 23)
+        q_cols("dy_t", dy)
+        del dy
+        w = W.expert_weights(E, 2 * F, H, 0.02, dev, seed + 24)
+        q, sc = m.quantize_rowwise(w.view(E * 2 * F, H))
+        t["w_gu"] = (q.view(E, 2 * F, H), sc.view(E, 2 * F, H // 32))
+        del w
+        w = W.expert_weights(E, H, F, 0.02, dev, seed + 25)
+        q, sc = m.quantize_rowwise(w.view(E * H, F))
+        t["w_d"] = (q.view(E, H, F), sc.view(E, H, F // 32))
+        del w
+        self.t = t
+        self.y_gu = torch.empty(self.M, 2 * F, dtype=torch.bfloat16, device=dev)
+        self.y_d = torch.empty(self.M, H, dtype=torch.bfloat16, device=dev)
+        self.dw_gu = torch.empty(E, 2 * F, H, dtype=torch.float32, device=dev)
+        self.dw_d = torch.empty(E, H, F, dtype=torch.float32, device=dev)
+        rows = sp.real_rows
+        self.flops = {"fwd_gate_up": 2 * rows * 2 * F * H, "fwd_down": 2 * rows * H * F,
+                      "wgrad_gate_up": 2 * rows * 2 * F * H, "wgrad_down": 2 * rows * H * F}
+        torch.cuda.synchronize()
+
+    def gemm_calls(self):
+        m = pkg()
+        L = m._lib.load()
+        E, H, F, M = MIX_E, MIX_HIDDEN, MIX_FFN, self.M
+        s = lambda: m._lib.stream_ptr()
+        chk = m._lib.check
+        t = self.t
+        dev = self.y_gu.device
+        calls = []
+
+        def fwd(name, a, w, N, K, out):
+            ws = torch.empty(L.mxg_grouped_fwd_workspace_size(E, M, N, K), dtype=torch.uint8, device=dev)
+            prep = lambda: chk(L.mxg_grouped_fwd_prepare(a[1].data_ptr(), w[1].data_ptr(), self.offs.data_ptr(),
+                                                         E, 1, E, M, N, K, ws.data_ptr(), ws.numel(), s()), "prep")
+            run = lambda: chk(L.mxg_grouped_fwd_run(a[0].data_ptr(), w[0].data_ptr(), E, M, N, K, out.data_ptr(),
+                                                    0, ws.data_ptr(), ws.numel(), s()), "run")
+            calls.append((name, prep, run, ws))
+
+        def wgrad(name, go, ia, N, K, out):
+            ws = torch.empty(L.mxg_grouped_wgrad_workspace_size(E, M, N, K), dtype=torch.uint8, device=dev)
+            prep = lambda: chk(L.mxg_grouped_wgrad_prepare(go[1].data_ptr(), ia[1].data_ptr(), self.sizes.data_ptr(),
+                                                           E, 2, E, M, N, K, ws.data_ptr(), ws.numel(), s()), "prep")
+            run = lambda: chk(L.mxg_grouped_wgrad_run(go[0].data_ptr(), ia[0].data_ptr(), E, M, N, K, out.data_ptr(),
+                                                      1, ws.data_ptr(), ws.numel(), s()), "run")
+            calls.append((name, prep, run, ws))
+
+        fwd("fwd_gate_up", t["x"], t["w_gu"], 2 * F, H, self.y_gu)
+        fwd("fwd_down", t["h"], t["w_d"], H, F, self.y_d)
+        wgrad("wgrad_gate_up", t["dgu_t"], t["x_t"], 2 * F, H, self.dw_gu)
+        wgrad("wgrad_down", t["dy_t"], t["h_t"], H, F, self.dw_d)
+        self._ws = [c[3] for c in calls]
+        return [c[:3] for c in calls]
+
+
+def measure_mixtral(args, world):
+    """Config 3 on one GPU: its four GEMM calls (prepare + kernel) per step."""
+    wl = MixtralWorkload(seed=args.seed)
+    calls = wl.gemm_calls()
+    steps = max(3, min(args.steps, 30))
+    ms_step, run_ms, prep_ms = time_steps(calls, steps, max(3, args.warmup), world)
+    code = pkg().device_error()
+    if code:
+        raise RuntimeError(f"device error {code} during the config-3 timed region")
+    tot = sum(wl.flops.values())
+    res = {"value": round(tot / (ms_step * 1e-3) / 1e12, 2), "unit": "TFLOPS",
+           "ms_per_step": round(ms_step, 4), "steps": steps,
+           "workload": "config 3 (Mixtral-shaped): 8 experts, 32768 tokens top-2 from softmax(N(0,1)), "
+                       "gate/up N=28672 K=4096 and down N=4096 K=14336, fwd + wgrad (fp32 dW)",
+           "routed_rows": wl.split.real_rows, "padded_rows": wl.M,
+           "per_kernel": {k: {"tflops_kernel": round(wl.flops[k] / (run_ms[k] * 1e-3) / 1e12, 1),
+                              "kernel_ms": round(run_ms[k], 4), "prepare_ms": round(prep_ms[k], 4)}
+                          for k in run_ms}}
+    del wl, calls
+    torch.cuda.empty_cache()
+    return res
+
 
 def time_steps(calls, steps, warmup, world):
     """Events around every prepare/run of every step; returns per-step total
@@ -700,6 +813,11 @@ def run_mxg(args, rank, world, local):
            "roofline": roofline, "quantize": quant, "cpu_baseline": cpu, "e2e": e2e,
            "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.values()),
            "clocks": clk.summary()}
+    if args.case == "dsv3" and not args.no_mixtral:
+        del wl, calls
+        torch.cuda.empty_cache()
+        out["mixtral_cfg3"] = measure_mixtral(args, world)
+        wl = calls = None
     if not args.no_ep and args.case == "dsv3":
         del wl, calls
         torch.cuda.empty_cache()
@@ -859,6 +977,7 @@ def main():
                     help="EP layer: run the dy dispatch and the combine's return beside the GEMMs "
                          "(measured slower on 8 B200s: the GEMMs lose more than the exchange hides)")
     ap.add_argument("--no-ep", action="store_true", help="N=1: skip the one-GPU EP layer measurement")
+    ap.add_argument("--no-mixtral", action="store_true", help="N=1: skip the config-3 (Mixtral-shaped) measurement")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
                     help="EP layer token exchange: NVLink peer stores or NCCL all_to_all")
     ap.add_argument("--p2p-blocks", type=int, default=0, help="grid cap of the peer-store kernels (0: default)")
