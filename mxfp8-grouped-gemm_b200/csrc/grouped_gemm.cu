@@ -972,7 +972,7 @@ __global__ void zero_tail_kernel(const int* meta, uint8_t* out, int64_t M, int64
 }
 
 // ---------------------------------------------------------------- host side
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -989,7 +989,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // 2-D uint8 operand [rows, cols] (cols contiguous), box {128 bytes, box_rows},
 // 128-byte swizzle; out-of-range elements read as zero.
 static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t cols, int box_rows) {
-  auto enc = get_encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return MXG_ERR_CUDA;
   cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
   cuuint64_t strides[1] = {cuuint64_t(cols)};
@@ -1007,7 +1007,7 @@ static int make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int64_t co
 // swizzle matches the staging layout (64-byte rows for bf16, 128 for fp32).
 static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, int out_dtype,
                              int box_rows) {
-  auto enc = get_encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return MXG_ERR_CUDA;
   const bool f32 = out_dtype == MXG_DTYPE_F32;
   const cuuint64_t esz = f32 ? 4 : 2;
@@ -1027,7 +1027,7 @@ static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, 
 // epilogue's staging layout).
 static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols,
                                int out_dtype, int row_bytes) {
-  auto enc = get_encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return MXG_ERR_CUDA;
   const bool f32 = out_dtype == MXG_DTYPE_F32;
   const cuuint64_t esz = f32 ? 4 : 2;
@@ -1044,7 +1044,7 @@ static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t r
 
 // dW [E, rows, cols] bf16, box {16 cols (32 B), 32 rows, 1}, no swizzle.
 static int make_out_tmap_wgrad16(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols) {
-  auto enc = get_encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return MXG_ERR_CUDA;
   cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(E)};
   cuuint64_t strides[2] = {cuuint64_t(cols) * 2, cuuint64_t(cols) * 2 * cuuint64_t(rows)};
@@ -1057,7 +1057,7 @@ static int make_out_tmap_wgrad16(CUtensorMap* tm, void* base, int64_t E, int64_t
 }
 
 static int make_sf_tmap(CUtensorMap* tm, const void* base, int64_t rows, int box_rows) {
-  auto enc = get_encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return MXG_ERR_CUDA;
   cuuint64_t dims[2] = {128, cuuint64_t(rows)};
   cuuint64_t strides[1] = {512};

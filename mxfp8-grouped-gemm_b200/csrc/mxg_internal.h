@@ -1,6 +1,8 @@
 // Host-side helpers shared by the library's translation units.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include "mxg.h"
@@ -21,5 +23,7 @@ int* device_error_word();
 int64_t take_injected_stall();
 // SMs the persistent GEMMs may use (0: all), set by mxg_set_gemm_sm_limit.
 int gemm_sm_limit();
+// The driver's cuTensorMapEncodeTiled (null when unavailable), looked up once.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 }  // namespace mxg

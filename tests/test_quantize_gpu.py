@@ -44,7 +44,7 @@ def test_rowwise_random_bit_exact(mxg, orc, cuda_dev, shape, scale):
     assert np.array_equal(q.view(torch.uint8).cpu().numpy(), oq)
 
 
-@pytest.mark.parametrize("shape", [(32, 2), (96, 1030), (2048, 512), (160, 7168)])
+@pytest.mark.parametrize("shape", [(32, 2), (96, 1030), (2048, 512), (160, 7168), (1056, 2080)])
 def test_colwise_random_bit_exact(mxg, orc, cuda_dev, shape):
     gen = torch.Generator(device=cuda_dev).manual_seed(11)
     x = torch.randn(*shape, generator=gen, device=cuda_dev).to(torch.bfloat16)
@@ -130,3 +130,18 @@ def test_swiglu_bwd_quantize_matches_unfused(mxg, cuda_dev, R, I):
     ref = mxg.ops.quantize_dual(mxg.ops.swiglu_bwd(gu, dh))
     for a, b in zip(fused, ref):
         assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
+@pytest.mark.parametrize("shape", [(1056, 2080), (4096, 7168)])
+def test_quantize_dual_partial_tiles_bits_match_oracle(mxg, orc, cuda_dev, shape):
+    """Both encodings in one pass on shapes with partial 128 x 128 tiles in
+    both directions (and whole ones), special values included: bit-exact
+    against the oracle."""
+    gen = torch.Generator(device=cuda_dev).manual_seed(shape[0] * 3 + shape[1])
+    x = _special_bf16(shape, gen, cuda_dev, scale=7.0)
+    q, s, qt, st = mxg.ops.quantize_dual(x)
+    bits = _bits(x)
+    rq, rs = orc.quantize_rowwise(bits)
+    cq, cs = orc.quantize_colwise(bits)
+    assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(q.view(torch.uint8).cpu().numpy(), rq)
+    assert np.array_equal(st.cpu().numpy(), cs) and np.array_equal(qt.view(torch.uint8).cpu().numpy(), cq)
