@@ -290,14 +290,17 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
   const int units = p.side == 0 ? p.E * 2 * mbp : ustart[p.E];
   // A thread packs rows q, q+32, q+64, q+96 of one 128-row half and stores
   // their four words as one 16-byte vector (a warp writes a whole 512-byte
-  // chunk half per k-block instead of scattering 4-byte words).
+  // chunk half per k-block instead of scattering 4-byte words).  A block
+  // takes one unit at a time; its thread groups split the unit's k-blocks
+  // (group ks takes ks, ks + KS, ...), which keeps each thread's chain of
+  // dependent loads short.
   const int rows_per_unit = p.side == 0 ? kBM : 2 * kBM;
-  const int tpu = rows_per_unit / 4;            // threads per unit
-  const int upb = int(blockDim.x) / tpu;        // units per block at a time
-  const int sub = int(threadIdx.x) / tpu, t = int(threadIdx.x) % tpu;
+  const int tpu = rows_per_unit / 4;            // threads per k-block of a unit
+  const int KS = int(blockDim.x) / tpu;         // k-split groups per unit
+  const int ks = int(threadIdx.x) / tpu, t = int(threadIdx.x) % tpu;
   const int half = t >> 5, q = t & 31;
   const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
-  for (int u = blockIdx.x * upb + sub; u < units; u += gridDim.x * upb) {
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
     int e, blk;
     if (p.side == 0) {
       e = u / (2 * mbp);
@@ -348,8 +351,8 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
       sh[j] = uint32_t(a & 3u) * 8u;
     }
     uint4* d = reinterpret_cast<uint4*>(p.dst + int64_t(chunk0) * chunk_bytes + half * 512 + q * 16);
-#pragma unroll 2
-    for (int kb = 0; kb < kbn; ++kb) {
+#pragma unroll 4
+    for (int kb = ks; kb < kbn; kb += KS) {
       const int col = col0 + kb * 4;
       uint32_t w[4];
 #pragma unroll
@@ -1173,12 +1176,18 @@ static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
   pb.src = reinterpret_cast<const uint8_t*>(b_sc);
   pb.dst = wsb + L.sfb_off;
   if (P.mode == MODE_FWD) {  // K/32-byte scale rows: word-aligned row walks
-    // 128 threads = four 128-row A units or two 256-row B units at a time
-    pack_scales_kernel<<<std::max(1, std::min((a_units + 3) / 4, sms * 16)), 128, 0, stream>>>(pa);
-    pack_scales_kernel<<<sms * 8, 128, 0, stream>>>(pb);
+    // 256 threads per unit: 8 k-split groups of a 128-row A unit, 4 of a
+    // 256-row B unit
+    pack_scales_kernel<<<std::max(1, std::min(a_units, sms * 16)), 256, 0, stream>>>(pa);
+    pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
   } else {
-    pack_scales_chunk_kernel<<<sms * 8, 128, 0, stream>>>(pa);
-    pack_scales_chunk_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+    // about one chunk half per warp (the chunk counts are bounded by the
+    // workspace layout), so each warp's loads go out in one round
+    const int64_t cap = int64_t(sms) * 64;
+    pack_scales_chunk_kernel<<<unsigned(std::max<int64_t>(1, std::min(cap, (L.sfa_chunks + 3) / 4))), 128, 0,
+                               stream>>>(pa);
+    pack_scales_chunk_kernel<<<unsigned(std::max<int64_t>(1, std::min(cap, (2 * L.sfb_chunks + 7) / 8))), 256, 0,
+                               stream>>>(pb);
   }
   return cuda_status(cudaGetLastError());
 }
