@@ -620,7 +620,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmSFA,
                         const __grid_constant__ CUtensorMap tmSFB,
                         const __grid_constant__ CUtensorMap tmOut,
-                        const __grid_constant__ CUtensorMap tmOut16, GemmArgs g) {
+                        const __grid_constant__ CUtensorMap tmOut16,
+                        const __grid_constant__ CUtensorMap tmOutAux, GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   SmemLayout& s = *reinterpret_cast<SmemLayout*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -896,33 +897,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                   make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
             issue_store(&tmOut16, smem_u32(epi), ti.n0 + c0, r0, ti.e, true);
           }
-        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && cols_here == 32) {
-          // bf16: row = lane, 32 columns (64 B), 64-byte swizzle
-          slot_ready();
-          uint8_t* buf = epi + slot * 2048;
+        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store) {
+          // bf16: row = lane.  Chunks pair up (columns [64j, 64j + 64) of the
+          // tile) into 128-byte rows, 128-byte swizzle, one store from the
+          // warp's whole 4 KiB buffer -- half the store requests of 64-byte
+          // rows.  A chunk without a full partner (the tile's last 32 or 16
+          // columns) leaves alone: 64-byte rows (64-byte swizzle) or 32-byte
+          // rows (unswizzled); the tensor edge clips every store.
+          const int r0 = ti.mb * kBM + warp * 32;
+          const int pair0 = c0 & ~63;
+          const bool paired = pair0 + 64 <= ti.nlen;
+          auto pack8 = [&](int u) {
+            return make_uint4(pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
+                              pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
+          };
+          if (paired) {
+            const int hc = (c0 - pair0) >> 3;  // 16-byte chunk offset of this half (8 bf16 each): 0 or 4
+            if (hc == 0 && epi_pending) {      // the previous store has read the buffer
+              if (lane == 0) bulk_wait_group_read0();
+              __syncwarp();
+            }
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            *reinterpret_cast<uint4*>(buf + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) = make_uint4(
-                pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
-          issue_store(&tmOut, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e, true);
-          slot ^= 1u;
-        } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && cols_here == 16) {
-          // bf16 remainder of a 240-column tile: row = lane, 16 columns (32 B),
-          // unswizzled rows (the store's box); the tensor edge clips it
-          slot_ready();
-          uint8_t* buf = epi + slot * 2048;
+            for (int u = 0; u < 4; ++u)
+              *reinterpret_cast<uint4*>(epi + lane * 128 + (((hc + u) ^ (lane & 7)) * 16)) = pack8(u);
+            if (hc != 0) issue_store(&tmOut, smem_u32(epi), ti.n0 + pair0, r0, ti.e, true);
+          } else {
+            if (epi_pending) {
+              if (lane == 0) bulk_wait_group_read0();
+              __syncwarp();
+            }
+            if (cols_here == 32) {
 #pragma unroll
-          for (int u = 0; u < 2; ++u)
-            *reinterpret_cast<uint4*>(buf + lane * 32 + u * 16) = make_uint4(
-                pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
-                pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
-          issue_store(&tmOut16, smem_u32(buf), ti.n0 + c0, ti.mb * kBM + warp * 32, ti.e, true);
-          slot ^= 1u;
+              for (int u = 0; u < 4; ++u)
+                *reinterpret_cast<uint4*>(epi + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) = pack8(u);
+              issue_store(&tmOut16, smem_u32(epi), ti.n0 + c0, r0, ti.e, true);
+            } else {
+#pragma unroll
+              for (int u = 0; u < 2; ++u) *reinterpret_cast<uint4*>(epi + lane * 32 + u * 16) = pack8(u);
+              issue_store(&tmOutAux, smem_u32(epi), ti.n0 + c0, r0, ti.e, true);
+            }
+          }
         } else {
           store_chunk<MODE>(g, ti, row, c0, v, false);
         }
@@ -1026,8 +1042,8 @@ static int make_out_tmap_fwd(CUtensorMap* tm, void* base, int64_t M, int64_t N, 
 }
 
 // dW [E, rows, cols] output, box {row_bytes of columns (64: 16 fp32 or 32
-// bf16; 128: 32 fp32), 32 rows, 1}, swizzle of the same width (the
-// epilogue's staging layout).
+// bf16; 128: 32 fp32 or 64 bf16), 32 rows, 1}, swizzle of the same width
+// (the epilogue's staging layout).
 static int make_out_tmap_wgrad(CUtensorMap* tm, void* base, int64_t E, int64_t rows, int64_t cols,
                                int out_dtype, int row_bytes) {
   auto enc = tensor_map_encoder();
@@ -1217,7 +1233,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   if (st) return st;
   st = make_sf_tmap(&tmSFB, wsb + L.sfb_off, std::max<int64_t>(2 * L.sfb_chunks, 2), 2);
   if (st) return st;
-  CUtensorMap tmOut = tmA, tmOut16 = tmA;  // epilogue store maps (unused ones stay dummies)
+  CUtensorMap tmOut = tmA, tmOut16 = tmA, tmOutAux = tmA;  // epilogue store maps (unused: dummies)
   const int64_t out_esz = out_dtype == MXG_DTYPE_F32 ? 4 : 2;
   // TMA stores need the output row stride to be a multiple of 16 bytes
   const bool wgrad_tma = P.mode == MODE_WGRAD && (P.n_ext * out_esz) % 16 == 0;
@@ -1227,10 +1243,12 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
       if (st) return st;
       st = make_out_tmap_wgrad(&tmOut16, out, P.E, P.n_out, P.n_ext, out_dtype, 64);
       if (st) return st;
-    } else {  // 32-column stores, 16-column remainders of bf16 tiles
-      st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype, 64);
+    } else {  // 64-column stores, 32- and 16-column remainders of bf16 tiles
+      st = make_out_tmap_wgrad(&tmOut, out, P.E, P.n_out, P.n_ext, out_dtype, 128);
       if (st) return st;
-      st = make_out_tmap_wgrad16(&tmOut16, out, P.E, P.n_out, P.n_ext);
+      st = make_out_tmap_wgrad(&tmOut16, out, P.E, P.n_out, P.n_ext, out_dtype, 64);
+      if (st) return st;
+      st = make_out_tmap_wgrad16(&tmOutAux, out, P.E, P.n_out, P.n_ext);
       if (st) return st;
     }
   }
@@ -1272,7 +1290,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   cfg.numAttrs = 1;
   cudaError_t e;
   if (P.mode == MODE_FWD) {
-    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, ga);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, tmOutAux, ga);
     if (e == cudaSuccess) {
       const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
       zero_tail_kernel<<<num_sms(), 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
@@ -1280,7 +1298,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
       e = cudaGetLastError();
     }
   } else {
-    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_WGRAD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, ga);
+    e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_WGRAD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, tmOutAux, ga);
   }
   return cuda_status(e);
 }
