@@ -1151,7 +1151,6 @@ static int configure_kernels(int* pairs) {
   return MXG_OK;
 }
 
-static constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per wait
 
 // Host launch is split in two halves that share the workspace:
 //   prepare: group scheduler + scale-factor packing (reads offs and scales)
@@ -1271,7 +1270,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   ga.ldo = ldo;
   ga.err = err;
   const int64_t stall = take_injected_stall();
-  ga.timeout_ns = stall > 0 ? uint64_t(stall) : kDefaultTimeoutNs;
+  ga.timeout_ns = stall > 0 ? uint64_t(stall) : kWaitLimitNs;
   ga.stall_test = stall > 0 ? 1 : 0;
   ga.fwd_tma_store = fwd_tma ? 1 : 0;
   ga.wgrad_tma_store = wgrad_tma ? 1 : 0;

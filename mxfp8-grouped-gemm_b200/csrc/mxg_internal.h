@@ -13,6 +13,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? MXG_OK : MXG_ERR_CUDA; }
 
+// Longest a single mbarrier wait of a kernel may take before it gives up
+// with MXG_ERR_DEVICE_TIMEOUT.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
 // Current device is an sm_100-class GPU (cached per device ordinal).
 int check_device();
 // SM count of the current device (cached).

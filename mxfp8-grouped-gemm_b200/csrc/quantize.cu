@@ -530,7 +530,7 @@ static int launch_dual(DualArgs a, void* stream) {
     CUtensorMap tm;
     int* err = device_error_word();
     if (per_sm > 0 && err && ncx * nry <= INT32_MAX && make_quant_tmap(&tm, a.a, a.rows, a.cols)) {
-      DualTmaArgs p{a, int(ncx), int(ncx * nry), err, 2000000000ull};
+      DualTmaArgs p{a, int(ncx), int(ncx * nry), err, kWaitLimitNs};
       const int64_t grid = std::min<int64_t>(ncx * nry, int64_t(num_sms()) * per_sm);
       quant_dual_tma_kernel<<<unsigned(grid), kQThreads, kQSmemBytes, (cudaStream_t)stream>>>(tm, p);
       return cuda_status(cudaGetLastError());
