@@ -410,17 +410,27 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
   dual_store_col_scales<KIND>(a, col_scales, r0, c0, t);
 }
 
-// Column-wise encode of a plain tensor: a persistent variant fed by TMA.
-// Each block (two per SM) keeps kQStages 32 KiB tiles in flight in a shared
-// memory ring: one thread issues a tile's 2-D bulk-tensor load as soon as
-// its slot is free, and the block runs the column pass above on the tile
-// that has landed, so the HBM reads never wait for the encode (5.6 instead of
-// 4.9 TB/s at 65536 x 7168).  With both encodings the register-fed kernel
-// above measured faster (4.1 vs 3.7-3.9 TB/s), so it keeps that case.  Tiles
-// go to blocks round-robin; the waits are bounded.
-constexpr int kQStages = 3;
-constexpr uint32_t kQTileBytes = uint32_t(kTileRows) * kTileCols * 2;  // 32 KiB
-constexpr size_t kQSmemBytes = size_t(kQStages) * kQTileBytes;
+// Column-wise encodes through a persistent variant fed by TMA.  Each block
+// (two per SM) keeps a ring of tiles in flight in shared memory: one thread
+// issues a tile's bulk-tensor loads as soon as its slot is free, and the
+// block runs the column pass above on the tile that has landed, so the HBM
+// reads never wait for the encode (plain tensors: 5.6 instead of 4.9 TB/s at
+// 65536 x 7168).  Plain: three 32 KiB stages of 128 x 128 bf16.  SwiGLU
+// gradient: two 48 KiB stages, each 128 rows x 64 of g and u (one 3-D box
+// over gu [R, 2, I], so a tile row is g then u, 256 bytes) plus the matching
+// 128 x 64 of dh; dg and du are computed in place over g and u, rounded to
+// bf16 as the unfused kernel rounds them.  With both encodings the
+// register-fed kernel above measured faster (plain: 4.1 vs 3.7-3.9 TB/s), so
+// it keeps that case.  Tiles go to blocks round-robin; the waits are bounded.
+template <int KIND>
+struct TmaTile {
+  static constexpr int kStages = KIND == DUAL_SWIGLU_GRAD ? 2 : 3;
+  static constexpr uint32_t kInBytes = uint32_t(kTileRows) * kTileCols * 2;   // the 128 x 128 tile
+  static constexpr uint32_t kDhBytes = KIND == DUAL_SWIGLU_GRAD ? uint32_t(kTileRows) * kTileCols : 0;
+  static constexpr uint32_t kStageBytes = kInBytes + kDhBytes;
+  static constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes;
+  static constexpr int kColsPerTile = KIND == DUAL_SWIGLU_GRAD ? kTileCols / 2 : kTileCols;
+};
 
 struct DualTmaArgs {
   DualArgs a;
@@ -432,68 +442,111 @@ struct DualTmaArgs {
 
 constexpr int kQThreads = 256;
 
-__global__ void __launch_bounds__(kQThreads, 2) quant_dual_tma_kernel(const __grid_constant__ CUtensorMap tm,
-                                                                       DualTmaArgs p) {
-  constexpr int R = kTileRows, CW = kTileCols / 2;
+template <int KIND>
+__global__ void __launch_bounds__(kQThreads, 2)
+    quant_dual_tma_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_dh,
+                          DualTmaArgs p) {
+  using T = TmaTile<KIND>;
+  constexpr int R = kTileRows, CW = kTileCols / 2, S = T::kStages;
   extern __shared__ __align__(128) uint8_t qsm[];
-  uint32_t(*tiles)[R][CW] = reinterpret_cast<uint32_t(*)[R][CW]>(qsm);
-  __shared__ uint64_t full[kQStages];
+  __shared__ uint64_t full[S];
   __shared__ int abort_flag;
   __shared__ __align__(4) uint8_t col_scales[kTileCols][R / 32];
   const int t = threadIdx.x;
   const DualArgs& a = p.a;
   const int grid = int(gridDim.x), b = int(blockIdx.x);
   const int my = p.ntiles > b ? (p.ntiles - b + grid - 1) / grid : 0;
+  auto tile_of = [&](int slot) { return reinterpret_cast<uint32_t(*)[CW]>(qsm + size_t(slot) * T::kStageBytes); };
+  auto dh_of = [&](int slot) {
+    return reinterpret_cast<const uint32_t(*)[CW / 2]>(qsm + size_t(slot) * T::kStageBytes + T::kInBytes);
+  };
   if (t == 0) {
-    for (int i = 0; i < kQStages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    for (int i = 0; i < S; ++i) mbar_init(smem_u32(&full[i]), 1);
     abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm);
+    if (KIND == DUAL_SWIGLU_GRAD) tma_prefetch_desc(&tm_dh);
   }
   __syncthreads();
   WaitCtl wc{&abort_flag, p.err, p.timeout_ns, 0u};
-  auto issue = [&](int j) {  // tile j of this block into slot j % kQStages
+  auto issue = [&](int j) {  // tile j of this block into slot j % S
     const int tt = b + j * grid;
-    const uint32_t bar = smem_u32(&full[j % kQStages]);
-    mbar_arrive_expect_tx(bar, kQTileBytes);
-    tma_load_2d(smem_u32(&tiles[j % kQStages][0][0]), &tm, (tt % p.ncx) * kTileCols, (tt / p.ncx) * R, bar);
+    const int x = (tt % p.ncx) * T::kColsPerTile, y = (tt / p.ncx) * R;
+    const uint32_t bar = smem_u32(&full[j % S]);
+    const uint32_t dst = smem_u32(qsm + size_t(j % S) * T::kStageBytes);
+    mbar_arrive_expect_tx(bar, T::kStageBytes);
+    if (KIND == DUAL_SWIGLU_GRAD) {
+      tma_load_3d(dst, &tm, x, 0, y, bar);                    // g and u: [128 rows][2][64]
+      tma_load_2d(dst + T::kInBytes, &tm_dh, x, y, bar);      // dh: [128 rows][64]
+    } else {
+      tma_load_2d(dst, &tm, x, y, bar);
+    }
   };
   if (t == 0)
-    for (int j = 0; j < kQStages && j < my; ++j) issue(j);
+    for (int j = 0; j < S && j < my; ++j) issue(j);
   int i = 0;
   for (; i < my; ++i) {
     const int tt = b + i * grid;
-    const int64_t r0 = int64_t(tt / p.ncx) * R, c0 = int64_t(tt % p.ncx) * kTileCols;
-    const bool ok = mbar_wait(smem_u32(&full[i % kQStages]), uint32_t(i / kQStages) & 1u, wc);
+    const int64_t r0 = int64_t(tt / p.ncx) * R, c0 = int64_t(tt % p.ncx) * T::kColsPerTile;
+    const bool ok = mbar_wait(smem_u32(&full[i % S]), uint32_t(i / S) & 1u, wc);
     if (__syncthreads_or(!ok)) break;
-    const uint32_t(*tile)[CW] = tiles[i % kQStages];
-    dual_column_pass<DUAL_PLAIN, kQThreads>(a, tile, col_scales, r0, c0, t);
+    uint32_t(*tile)[CW] = tile_of(i % S);
+    if (KIND == DUAL_SWIGLU_GRAD) {  // g, u -> dg, du in place (a warp per tile row per step)
+      const uint32_t(*dh)[CW / 2] = dh_of(i % S);
+#pragma unroll 4
+      for (int k = t; k < R * (CW / 2); k += kQThreads) {
+        const int r = k / (CW / 2), w = k % (CW / 2);
+        uint32_t dg, du;
+        swiglu_grad_word(tile[r][w], tile[r][CW / 2 + w], dh[r][w], dg, du);
+        tile[r][w] = dg;
+        tile[r][CW / 2 + w] = du;
+      }
+      __syncthreads();
+    }
+    dual_column_pass<KIND, kQThreads>(a, tile, col_scales, r0, c0, t);
     __syncthreads();
-    dual_store_col_scales<DUAL_PLAIN>(a, col_scales, r0, c0, t);
+    dual_store_col_scales<KIND>(a, col_scales, r0, c0, t);
     __syncthreads();  // the slot and col_scales are free again
-    if (t == 0 && i + kQStages < my) issue(i + kQStages);
+    if (t == 0 && i + S < my) issue(i + S);
   }
   if (i < my && t == 0) {  // gave up: let the loads still in flight land before the block exits
-    for (int j = i; j < my && j < i + kQStages; ++j)
-      mbar_drain(smem_u32(&full[j % kQStages]), uint32_t(j / kQStages) & 1u, 20000000ull);
+    for (int j = i; j < my && j < i + S; ++j)
+      mbar_drain(smem_u32(&full[j % S]), uint32_t(j / S) & 1u, 20000000ull);
   }
 }
 
-// Tensor map of a bf16 [rows, cols] tensor with 128 x 128 boxes (no swizzle,
-// out-of-range elements read as zero).
-static bool make_quant_tmap(CUtensorMap* tm, const void* x, int64_t rows, int64_t cols) {
+// Tensor maps (no swizzle, out-of-range elements read as zero).  Plain: bf16
+// [rows, cols] with 128 x 128 boxes.  SwiGLU gradient: gu [rows, 2, inter]
+// with {64, 2, 128} boxes and dh [rows, inter] with 64 x 128 boxes.
+static bool make_quant_tmaps(int kind, const DualArgs& a, CUtensorMap* tm, CUtensorMap* tm_dh) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
-  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
-  cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
-  cuuint32_t box[2] = {cuuint32_t(kTileCols), cuuint32_t(kTileRows)};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  cuuint32_t estr[3] = {1, 1, 1};
+  if (kind == DUAL_PLAIN) {
+    cuuint64_t dims[2] = {cuuint64_t(a.cols), cuuint64_t(a.rows)};
+    cuuint64_t strides[1] = {cuuint64_t(a.cols) * 2};
+    cuuint32_t box[2] = {cuuint32_t(kTileCols), cuuint32_t(kTileRows)};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint4*>(a.a), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  cuuint64_t dims3[3] = {cuuint64_t(a.inter), 2, cuuint64_t(a.rows)};
+  cuuint64_t strides3[2] = {cuuint64_t(a.inter) * 2, cuuint64_t(a.inter) * 4};
+  cuuint32_t box3[3] = {cuuint32_t(kTileCols / 2), 2, cuuint32_t(kTileRows)};
+  if (enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint4*>(a.a), dims3, strides3, box3, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  cuuint64_t dims2[2] = {cuuint64_t(a.inter), cuuint64_t(a.rows)};
+  cuuint64_t strides2[1] = {cuuint64_t(a.inter) * 2};
+  cuuint32_t box2[2] = {cuuint32_t(kTileCols / 2), cuuint32_t(kTileRows)};
+  return enc(tm_dh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint4*>(a.dh), dims2, strides2, box2, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static int quant_tma_blocks_per_sm() {  // per device: shared-memory attribute set once
+template <int KIND>
+static int quant_tma_blocks_per_sm() {  // per device and kind: shared-memory attribute set once
   static std::mutex mu;
   static int ready[64] = {0};
   int dev = 0;
@@ -501,15 +554,43 @@ static int quant_tma_blocks_per_sm() {  // per device: shared-memory attribute s
   std::lock_guard<std::mutex> lk(mu);
   if (ready[dev] == 0) {
     ready[dev] = -1;
-    if (cudaFuncSetAttribute(quant_dual_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(kQSmemBytes)) == cudaSuccess) {
+    const size_t smem = TmaTile<KIND>::kSmemBytes;
+    if (cudaFuncSetAttribute(quant_dual_tma_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(smem)) == cudaSuccess) {
       int n = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_dual_tma_kernel, kQThreads, kQSmemBytes) ==
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_dual_tma_kernel<KIND>, kQThreads, smem) ==
               cudaSuccess && n > 0)
         ready[dev] = n;
     }
   }
   return ready[dev] > 0 ? ready[dev] : 0;
+}
+
+// Column-wise-only plain and SwiGLU-gradient encodes through the TMA kernel;
+// returns false (nothing launched) when that path does not apply.
+template <int KIND>
+static bool launch_dual_tma(const DualArgs& a, void* stream, int* status) {
+  if constexpr (KIND == DUAL_SWIGLU) {
+    return false;
+  } else {
+    if (a.q != nullptr) return false;
+    if (KIND == DUAL_SWIGLU_GRAD && (a.inter % 32 != 0 || !aligned16(a.dh))) return false;
+    const int per_sm = quant_tma_blocks_per_sm<KIND>();
+    const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
+    const int64_t ncx = (span + TmaTile<KIND>::kColsPerTile - 1) / TmaTile<KIND>::kColsPerTile;
+    const int64_t nry = (a.rows + kTileRows - 1) / kTileRows;
+    CUtensorMap tm, tm_dh;
+    int* err = device_error_word();
+    if (per_sm <= 0 || !err || ncx * nry > INT32_MAX) return false;
+    if (!make_quant_tmaps(KIND, a, &tm, &tm_dh)) return false;
+    if (KIND == DUAL_PLAIN) tm_dh = tm;  // unused
+    DualTmaArgs p{a, int(ncx), int(ncx * nry), err, kWaitLimitNs};
+    const int64_t grid = std::min<int64_t>(ncx * nry, int64_t(num_sms()) * per_sm);
+    quant_dual_tma_kernel<KIND><<<unsigned(grid), kQThreads, TmaTile<KIND>::kSmemBytes,
+                                  (cudaStream_t)stream>>>(tm, tm_dh, p);
+    *status = cuda_status(cudaGetLastError());
+    return true;
+  }
 }
 
 template <int KIND>
@@ -524,18 +605,8 @@ static int launch_dual(DualArgs a, void* stream) {
   if ((a.rows + kTileRows - 1) / kTileRows > 65535) return MXG_ERR_BAD_SHAPE;
   int e = check_device();
   if (e) return e;
-  if (KIND == DUAL_PLAIN && a.q == nullptr) {
-    const int per_sm = quant_tma_blocks_per_sm();
-    const int64_t ncx = (a.cols + kTileCols - 1) / kTileCols, nry = (a.rows + kTileRows - 1) / kTileRows;
-    CUtensorMap tm;
-    int* err = device_error_word();
-    if (per_sm > 0 && err && ncx * nry <= INT32_MAX && make_quant_tmap(&tm, a.a, a.rows, a.cols)) {
-      DualTmaArgs p{a, int(ncx), int(ncx * nry), err, kWaitLimitNs};
-      const int64_t grid = std::min<int64_t>(ncx * nry, int64_t(num_sms()) * per_sm);
-      quant_dual_tma_kernel<<<unsigned(grid), kQThreads, kQSmemBytes, (cudaStream_t)stream>>>(tm, p);
-      return cuda_status(cudaGetLastError());
-    }
-  }
+  int tma_status = MXG_OK;
+  if (launch_dual_tma<KIND>(a, stream, &tma_status)) return tma_status;
   const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
   const int64_t per = KIND == DUAL_SWIGLU_GRAD ? kTileCols / 2 : kTileCols;
   dim3 grid(unsigned((span + per - 1) / per), unsigned((a.rows + kTileRows - 1) / kTileRows));
