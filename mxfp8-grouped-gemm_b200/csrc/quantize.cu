@@ -233,7 +233,11 @@ __device__ __forceinline__ void encode_row_chunk(const DualArgs& a, uint4 v, int
 // 2p+1, share the block amax with one shuffle, and store their 16 bytes of
 // each column side by side, so one store instruction writes whole 32-byte
 // sectors of the transposed output.  Block scales go to col_scales.
-template <int KIND, int NT = 256>
+// SWZ: the tile was staged with rows 16-31 of every 32-row block shifted by
+// 16 words (16-byte chunk c stored at c ^ 4), so the two lanes of a pair,
+// 16 rows apart, read different banks (register-fed kernel; TMA-fed tiles
+// keep the plain layout).
+template <int KIND, int NT = 256, bool SWZ = false>
 __device__ __forceinline__ void dual_column_pass(const DualArgs& a, const uint32_t (*tile)[kTileCols / 2],
                                                  uint8_t (*col_scales)[kTileRows / 32], int64_t r0,
                                                  int64_t c0, int t) {
@@ -254,7 +258,7 @@ __device__ __forceinline__ void dual_column_pass(const DualArgs& a, const uint32
       col_ok = col0 < a.cols;
     }
     // (the partner lane always has the same rblk and pcol: same predicate)
-    const uint32_t* colp = &tile[32 * rblk + 16 * h][pcol];
+    const uint32_t* colp = &tile[32 * rblk + 16 * h][SWZ ? (pcol ^ (h << 4)) : pcol];
     uint32_t w[16];
     uint32_t m0 = 0, m1 = 0;
 #pragma unroll
@@ -367,7 +371,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
       const int64_t col = c0 + ch * 8;
       const bool valid = col < a.cols && r0 + r < a.rows;
       if (a.q) encode_row_chunk(a, v[i], r0 + r, col, valid);
-      *reinterpret_cast<uint4*>(&tile[r][ch * 4]) = v[i];
+      *reinterpret_cast<uint4*>(&tile[r][(ch ^ (((r >> 4) & 1) << 2)) * 4]) = v[i];
     }
   } else {
     constexpr int JCPR = CPR / 2;  // input chunks per tile row (each yields a dg and a du chunk)
@@ -399,13 +403,14 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
         encode_row_chunk(a, dg[i], r0 + r, j, valid);
         encode_row_chunk(a, du[i], r0 + r, a.inter + j, valid);
       }
-      *reinterpret_cast<uint4*>(&tile[r][ch * 4]) = dg[i];
-      *reinterpret_cast<uint4*>(&tile[r][CW / 2 + ch * 4]) = du[i];
+      const int sw = ((r >> 4) & 1) << 2;  // see dual_column_pass<.., SWZ>
+      *reinterpret_cast<uint4*>(&tile[r][(ch ^ sw) * 4]) = dg[i];
+      *reinterpret_cast<uint4*>(&tile[r][((CW / 8 + ch) ^ sw) * 4]) = du[i];
     }
   }
   if (a.qt == nullptr) return;
   __syncthreads();
-  dual_column_pass<KIND>(a, tile, col_scales, r0, c0, t);
+  dual_column_pass<KIND, 256, true>(a, tile, col_scales, r0, c0, t);
   __syncthreads();
   dual_store_col_scales<KIND>(a, col_scales, r0, c0, t);
 }
