@@ -13,7 +13,7 @@ the reference-facing API (group scheduler + scale packing + tensor-core
 kernel).  ``value`` = algorithmic FLOPs (2 * real rows * N * K) / time.
 All operands together exceed the 126 MB L2, so no explicit flush is needed.
 
-N>1 (torchrun, one rank per GPU): BASELINE config 5, the DeepSeek-V3 MoE
+N>1 (torchrun, one rank per GPU): BASELINE config 4, the DeepSeek-V3 MoE
 expert layer under expert parallelism.  256 experts are sharded evenly (256/N
 per GPU, placed by expected load), each GPU routes 16384 tokens top-8 with
 Zipf(1.1) expert popularity, and one step is NCCL all-to-all dispatch ->
@@ -541,7 +541,7 @@ def sample_experts(wl, n=2):
 
 
 
-# ---------------------------------------------------------------- EP layer (config 5)
+# ---------------------------------------------------------------- EP layer (config 4)
 EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
 # our kernels per layer step (NCCL's own kernels not counted): fused
 # quantisations 4 (x, swiglu, dy, swiglu backward), grouped fwd 3 x 5,
@@ -555,7 +555,7 @@ EP_LAUNCHES_PER_STEP = {"p2p": 4 + 15 + 8 + 3 + 2 + 2 + 2 + 1 + 1,
 
 
 class EpLayerBench:
-    """One rank's share of the config-5 layer: resident tokens, routing,
+    """One rank's share of the config-4 layer: resident tokens, routing,
     gradients and its local experts."""
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
@@ -657,7 +657,7 @@ def gather_over_ranks(v, world):
 
 
 def measure_ep_layer(lb, world, steps, warmup):
-    """Timed config-5 layer steps on this process group (every rank takes the
+    """Timed config-4 layer steps on this process group (every rank takes the
     same collective steps)."""
     ms, seg, plan = time_ep_layer(lb, steps, warmup, world)
     code = pkg().device_error()
@@ -687,7 +687,7 @@ def measure_ep_layer(lb, world, steps, warmup):
 
 
 def run_ep_mxg(args, rank, world, local):
-    """The N>1 bench line: config 5 across the process group."""
+    """The N>1 bench line: config 4 across the process group."""
     pkg()._lib.load()
     lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
                       transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
@@ -704,7 +704,7 @@ def run_ep_mxg(args, rank, world, local):
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
            "data": "synthetic",
-           "config": {"workload": "dsv3_ep_layer (config 5): dispatch, quantize, gate/up fwd, swiglu, "
+           "config": {"workload": "dsv3_ep_layer (config 4): dispatch, quantize, gate/up fwd, swiglu, "
                                   "down fwd, combine + down dgrad and both wgrads",
                       "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
                       "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
@@ -827,7 +827,7 @@ def run_mxg(args, rank, world, local):
         del lb
         out["ep_layer_1gpu"] = {"value": round(r["value"], 2), "unit": "TFLOPS",
                                 "ms_per_step": round(r["ms_per_step"], 4),
-                                "note": "config 5 layer on one GPU (all 256 experts, 16384 tokens): "
+                                "note": "config 4 layer on one GPU (all 256 experts, 16384 tokens): "
                                         "the same per-GPU work as each rank of the N>1 lines",
                                 "dw_dtype": args.ep_wgrad_dtype,
                                 "gemm_tflops": r["gemm_tflops_rank0"],
@@ -838,7 +838,7 @@ def run_mxg(args, rank, world, local):
 
 
 def cpu_reference_layer_sample(host, threads):
-    """The reference's torch path for the five GEMMs of the config-5 layer on
+    """The reference's torch path for the five GEMMs of the config-4 layer on
     the host (dequantise in fp32, fp32 matmul), for the sampled experts."""
     from oracle import mxfp8_oracle as orc
     torch.set_num_threads(threads)
@@ -859,7 +859,7 @@ def cpu_reference_layer_sample(host, threads):
 
 
 def run_reference_layer(args, world):
-    """Reference arm at N>1: the config-5 layer's GEMMs on the host for the
+    """Reference arm at N>1: the config-4 layer's GEMMs on the host for the
     two median-loaded experts (rows as the routing sends them per step)."""
     m = pkg()
     threads = os.cpu_count() or 1
@@ -891,14 +891,14 @@ def run_reference_layer(args, world):
         tot_fl += fl
         tot_dt += dt
     v = tot_fl / tot_dt / 1e12
-    sample = (f"per step experts {experts} ({[h['rows'] for h in host]} rows) of the config-5 layer: "
+    sample = (f"per step experts {experts} ({[h['rows'] for h in host]} rows) of the config-4 layer: "
               "gate/up fwd, down fwd, down dgrad, both wgrads; torch fp32 dequantise+matmul "
               "(reference fused_fwd.py:249-264, scale_correctness.py:110-137); no all-to-all (one host)")
     out = {"metric": METRIC, "value": round(v, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(1e3 * tot_dt / args.steps, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": "synthetic", "impl": "reference",
-           "config": {"workload": "dsv3_ep_layer (config 5) GEMMs, CPU sample",
+           "config": {"workload": "dsv3_ep_layer (config 4) GEMMs, CPU sample",
                       "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
                       "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "hidden": HIDDEN,
                       "intermediate": INTER, "parallelism": f"ep{world}"},
@@ -982,7 +982,7 @@ def main():
                     help="EP layer token exchange: NVLink peer stores or NCCL all_to_all")
     ap.add_argument("--p2p-blocks", type=int, default=0, help="grid cap of the peer-store kernels (0: default)")
     ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
-                    help="weight-gradient dtype of the config-5 expert layer (bf16: the reference's "
+                    help="weight-gradient dtype of the config-4 expert layer (bf16: the reference's "
                          "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
     ap.add_argument("--reserve-sms", type=int, default=0,
                     help="EP layer with --overlap: SMs kept free of GEMM blocks for the peer copies")
