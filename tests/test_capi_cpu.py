@@ -1,9 +1,6 @@
 """The C-ABI library on a machine without a GPU: it loads, exports every
 symbol include/mxg.h declares, and rejects bad arguments on the host before
 any CUDA call."""
-import ctypes
-
-import pytest
 
 
 def test_library_loads_and_exports_header_symbols(mxg):
