@@ -82,17 +82,100 @@ def max_over_ranks(v, world):
 
 
 # ---------------------------------------------------------------- peaks / clocks
+# A timed region shorter than this runs at the clocks of a burst (the power
+# cap has not pulled the SM clock down yet): the roofline then divides by the
+# burst peak; a longer one by the sustained peak.
+SUSTAINED_REGION_S = 2.0
+FP8_PEAK_FILE = os.path.join(REPO, "profiles", "fp8_peak_cublas_mxfp8.json")
+
+
 def peaks():
+    """Roofline denominators.  FP8: 2 x the driver-measured cuBLAS bf16
+    figures (MEASURED_PEAKS.json has no FP8 entry; FP8 dense is twice bf16
+    dense on this part), burst and sustained; the measured cuBLAS MXFP8
+    figures (``--fp8-peak`` mode, committed under profiles/) ride along."""
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         p = json.load(open(path))
-        return {"fp8_tflops": 2.0 * p["bf16_tflops_sustained"],
-                "fp8_tflops_burst": 2.0 * p["bf16_tflops"],
-                "hbm_gbs": p["hbm_gbs"],
-                "source": "2 x measured cuBLAS bf16 (MEASURED_PEAKS.json has no fp8 entry); "
-                          "sustained figure (kernels timed inside a long step)"}
-    return {"fp8_tflops": 2.0 * 1400.0, "fp8_tflops_burst": 2.0 * 1590.0, "hbm_gbs": 6650.0,
-            "source": "fallback: 2 x 1.4 PFLOP/s sustained bf16, 6.65 TB/s"}
+        out = {"fp8_tflops_burst": 2.0 * p["bf16_tflops"],
+               "fp8_tflops_sustained": 2.0 * p["bf16_tflops_sustained"],
+               "hbm_gbs": p["hbm_gbs"], "source": "of measured: 2 x cuBLAS bf16 from MEASURED_PEAKS.json"}
+    else:
+        out = {"fp8_tflops_burst": 2.0 * 1590.0, "fp8_tflops_sustained": 2.0 * 1400.0,
+               "hbm_gbs": 6650.0, "source": "of fallback: 2 x 1.59 (burst) / 1.4 (sustained) PFLOP/s bf16"}
+    if os.path.exists(FP8_PEAK_FILE):
+        try:
+            c = json.load(open(FP8_PEAK_FILE))
+            out["cublas_mxfp8_burst"] = c.get("tflops_burst")
+            out["cublas_mxfp8_sustained"] = c.get("tflops_sustained")
+        except Exception:
+            pass
+    return out
+
+
+def tensor_roofline(achieved, region_s, pk, **extra):
+    """The roofline object for a tensor-core kernel timed inside a region of
+    region_s seconds: burst peak below SUSTAINED_REGION_S, sustained above."""
+    burst = region_s < SUSTAINED_REGION_S
+    peak = pk["fp8_tflops_burst"] if burst else pk["fp8_tflops_sustained"]
+    r = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+         "frac": round(achieved / peak, 4),
+         "peak_kind": ("burst" if burst else "sustained") + f" (timed region {region_s:.2f} s)",
+         "peak_source": pk["source"]}
+    c = pk.get("cublas_mxfp8_burst" if burst else "cublas_mxfp8_sustained")
+    if c:
+        r["frac_of_cublas_mxfp8"] = round(achieved / c, 4)
+        r["cublas_mxfp8_tflops"] = c
+    r.update(extra)
+    return r
+
+
+def measure_fp8_peak(args):
+    """cuBLAS MXFP8 throughput on this GPU (torch._scaled_mm, e4m3 operands
+    from N(0,1), E8M0 block scales of 1.0): best of 10 at 8192^3 (burst) and
+    back to back for ~4 s (sustained), clocks sampled meanwhile."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    res = {"what": "torch._scaled_mm MXFP8 (e4m3 x e4m3, E8M0 1x32 block scales), bf16 out"}
+    for n in (8192, 16384):
+        g = torch.Generator(device=dev).manual_seed(n)
+        a = torch.randn(n, n, generator=g, device=dev).clamp_(-8, 8).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, generator=g, device=dev).clamp_(-8, 8).to(torch.float8_e4m3fn)
+        sa = torch.full((n * n // 32,), 1.0, device=dev).to(torch.float8_e8m0fnu)
+        sb = torch.full((n * n // 32,), 1.0, device=dev).to(torch.float8_e8m0fnu)
+        fn = lambda: torch._scaled_mm(a, b.t(), sa, sb, out_dtype=torch.bfloat16)
+        try:
+            fn()
+            torch.cuda.synchronize()
+        except Exception as e:  # record why (API/layout) instead of failing the run
+            res[f"n{n}_error"] = str(e).splitlines()[0][:300]
+            continue
+        flop = 2.0 * n ** 3
+        best = float("inf")
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e))
+        res[f"n{n}_burst_tflops"] = round(flop / (best * 1e-3) / 1e12, 1)
+        reps = max(1, int(4.0 / (best * 1e-3)))
+        with ClockSampler(0) as clk:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(reps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / reps
+        res[f"n{n}_sustained_tflops"] = round(flop / (ms * 1e-3) / 1e12, 1)
+        res[f"n{n}_sustained_s"] = round(reps * ms * 1e-3, 2)
+        res[f"n{n}_clocks"] = clk.summary()
+        del a, b
+    res["tflops_burst"] = res.get("n8192_burst_tflops")
+    res["tflops_sustained"] = res.get("n8192_sustained_tflops")
+    print(json.dumps(res), flush=True)
 
 
 class ClockSampler:
@@ -543,33 +626,52 @@ def sample_experts(wl, n=2):
 
 # ---------------------------------------------------------------- EP layer (config 4)
 EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
-# our kernels per layer step (NCCL's own kernels not counted): fused
-# quantisations 4 (x, swiglu, dy, swiglu backward), grouped fwd 3 x 5,
-# wgrad 2 x 4, plus the exchange:
+# our kernels per layer step (NCCL's own kernels and torch's small index
+# fills not counted): fused quantisations 4 (x, swiglu, dy, swiglu
+# backward), grouped fwd 4 x 5 (gate/up, down, down dgrad, gate/up dgrad),
+# wgrad 2 x 4, two combines, plus the exchange:
 #   p2p:  route 3, plan 2, zero pad + peer dispatch 2, dy zero pad + peer
-#         dispatch 2, peer return 1, combine 1
-#   nccl: route 3, send gather + regroup + gather 3, dy gathers 2, return
-#         gather 1, combine 1
-EP_LAUNCHES_PER_STEP = {"p2p": 4 + 15 + 8 + 3 + 2 + 2 + 2 + 1 + 1,
-                        "nccl": 4 + 15 + 8 + 3 + 3 + 2 + 1 + 1}
+#         dispatch 2, y and dx peer returns 2
+#   nccl: route 3, send gather + regroup + gather 3, dy gathers 2, y and dx
+#         return gathers 2
+EP_LAUNCHES_PER_STEP = {"p2p": 4 + 20 + 8 + 2 + 3 + 2 + 2 + 2 + 2,
+                        "nccl": 4 + 20 + 8 + 2 + 3 + 3 + 2 + 2}
+EXCHANGE_SEGMENTS = ("dispatch_x", "dispatch_dy", "return_y", "return_dx")
+
+
+def rank0_like_popularity(seed, world=8):
+    """Log-popularity of the 32 experts that balanced placement puts on rank
+    0 of an 8-GPU run of config 4: one GPU with these experts and 16384
+    tokens top-8 carries the same per-GPU load as a rank at N=8 (about
+    131072 routed rows over 32 experts, the same spread of group sizes)."""
+    m = pkg()
+    W = m.workloads
+    logp = W.zipf_log_popularity(EP_EXPERTS, EP_ZIPF, seed)
+    slot = m.ep.balanced_placement(W.expected_expert_load(logp, EP_TOPK), world)
+    mine = np.sort(np.nonzero(slot // (EP_EXPERTS // world) == 0)[0])
+    return logp[mine]
 
 
 class EpLayerBench:
     """One rank's share of the config-4 layer: resident tokens, routing,
-    gradients and its local experts."""
+    gradients and its local experts.  experts/logp override the expert set
+    (the one-GPU weak-scaling base uses rank 0's 32 experts of an 8-GPU run)."""
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
-                 transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16"):
+                 transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16", experts=EP_EXPERTS,
+                 logp=None, compute_dx=True):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
-        logp = W.zipf_log_popularity(EP_EXPERTS, EP_ZIPF, seed)
-        ids = W.zipf_topk_sample(tokens, logp, EP_TOPK, seed=seed * 7919 + 1 + rank)
+        self.seed, self.rank, self.world, self.num_experts = seed, rank, world, experts
+        self.logp = W.zipf_log_popularity(experts, EP_ZIPF, seed) if logp is None else logp
+        ids = W.zipf_topk_sample(tokens, self.logp, EP_TOPK, seed=seed * 7919 + 1 + rank)
         slot = None
         if placement == "balanced" and world > 1:
-            slot = m.ep.balanced_placement(W.expected_expert_load(logp, EP_TOPK), world)
+            slot = m.ep.balanced_placement(W.expected_expert_load(self.logp, EP_TOPK), world)
+        self.slot = slot
         self.placement = placement if world > 1 else "single"
-        self.ep = m.ExpertParallel(EP_EXPERTS, placement=slot, transport=transport,
+        self.ep = m.ExpertParallel(experts, placement=slot, transport=transport,
                                    p2p_max_blocks=p2p_blocks)
         g = torch.Generator(device=dev).manual_seed(seed * 1000 + 17 + rank)
         self.x = torch.randn(tokens, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16)
@@ -584,7 +686,7 @@ class EpLayerBench:
         self.wgrad_dtype = wgrad_dtype
         self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm,
                                      wgrad_dtype=torch.float32 if wgrad_dtype == "fp32" else torch.bfloat16,
-                                     reserve_sms=reserve_sms)
+                                     reserve_sms=reserve_sms, compute_dx=compute_dx)
         del w_gu, w_d
         torch.cuda.synchronize()
 
@@ -592,12 +694,15 @@ class EpLayerBench:
         return self.layer.step(self.x if x is None else x, self.ids if ids is None else ids,
                                self.probs if probs is None else probs, self.dy if dy is None else dy)
 
+    def close(self):
+        self.ep.close()
+
 
 def time_ep_layer(lb, steps, warmup, world):
     """Events on the main stream around K layer steps (the comm stream joins
     the main stream inside every step), plus per-segment marks."""
     for _ in range(warmup):
-        out = lb.step()
+        lb.step()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -605,7 +710,7 @@ def time_ep_layer(lb, steps, warmup, world):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
-        out, dw_gu, dw_d, plan = lb.step()
+        res = lb.step()
     end.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -617,26 +722,29 @@ def time_ep_layer(lb, steps, warmup, world):
         if b == "start":
             continue
         seg[b] = seg.get(b, 0.0) + ea.elapsed_time(eb) / steps
-    return ms, seg, plan
+    return ms, seg, res.plan
 
 
 def e2e_ep_layer(lb, steps):
     """Through the public API with host buffers: pinned x, dy, expert ids and
-    router probs -> H2D -> layer step -> D2H of the combined output, the
-    copies pipelined against the compute (pipelined_e2e)."""
+    router probs -> H2D -> layer step -> D2H of the combined output and of
+    the input gradient, the copies pipelined against the compute
+    (pipelined_e2e)."""
     host = {k: torch.empty(getattr(lb, k).shape, dtype=getattr(lb, k).dtype, pin_memory=True)
             for k in ("x", "ids", "probs", "dy")}
     for k, h in host.items():
         h.copy_(getattr(lb, k))
-    out_h = torch.empty(lb.x.shape, dtype=torch.bfloat16, pin_memory=True)
+    outs_h = [torch.empty(lb.x.shape, dtype=torch.bfloat16, pin_memory=True)]
+    if lb.layer.compute_dx:
+        outs_h.append(torch.empty(lb.x.shape, dtype=torch.bfloat16, pin_memory=True))
     h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_h.numel() * out_h.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in outs_h)
 
     def compute(d):
-        out, _, _, _ = lb.step(d["x"], d["ids"], d["probs"], d["dy"])
-        return (out,)
+        r = lb.step(d["x"], d["ids"], d["probs"], d["dy"])
+        return (r.out, r.dx) if lb.layer.compute_dx else (r.out,)
 
-    return pipelined_e2e(host, compute, [out_h], steps), h2d, d2h
+    return pipelined_e2e(host, compute, outs_h, steps), h2d, d2h
 
 
 def sum_over_ranks(v, world):
@@ -671,27 +779,189 @@ def measure_ep_layer(lb, world, steps, warmup):
     gemm_ms = {k: seg[k] for k in flops}
     dom = max(gemm_ms, key=lambda k: gemm_ms[k])
     achieved = flops[dom] / (gemm_ms[dom] * 1e-3) / 1e12
+    exch = {k: round(seg[k], 4) for k in EXCHANGE_SEGMENTS if k in seg}
     return {"value": flops_all / (ms_max * 1e-3) / 1e12, "ms_per_step": ms_max,
             "ms_per_step_this_rank": ms, "flops_per_step_all_ranks": flops_all,
+            "flops_per_step_this_rank": sum(flops.values()),
             "recv_rows_per_rank": {"max": max(rows), "mean": sum(rows) / len(rows), "min": min(rows)},
             "padded_rows_this_rank": int(sum(plan.group_rows_host)),
             "segments_ms_rank0": {k: round(v, 4) for k, v in seg.items()},
+            "exchange_ms_rank0": round(sum(exch.values()), 4) if lb.comm is None else None,
+            "gemm_ms_rank0": round(sum(gemm_ms.values()), 4),
             "gemm_tflops_rank0": {k: round(flops[k] / (gemm_ms[k] * 1e-3) / 1e12, 1) for k in flops},
-            "roofline": {"bound": "tensor", "kernel": f"grouped_gemm_kernel ({dom}, EP layer)",
-                         "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1),
-                         "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
-                         "peak_source": pk["source"], "traffic": None,
-                         "flops_per_launch": flops[dom]},
+            "roofline": tensor_roofline(achieved, ms * steps * 1e-3, pk,
+                                        kernel=f"grouped_gemm_kernel ({dom}, EP layer)",
+                                        traffic=None, flops_per_launch=flops[dom]),
             "placement": lb.placement, "overlap": lb.comm is not None, "transport": lb.ep.transport,
             "reserve_sms": lb.layer.reserve}
 
 
+# ---------------------------------------------------------------- EP layer verification
+VERIFY_TOKENS = 64      # tokens per rank of the verification slice
+VERIFY_SAMPLES = 256    # sampled output entries per GEMM
+
+
+def _bf16_np(a):
+    """float32 numpy -> (bf16 torch tensor, its exact float64 values)."""
+    t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16)
+    return t, t.float().numpy().astype(np.float64)
+
+
+def verify_ep_layer(lb, world, rank, seed=0):
+    """One layer step of lb on a seeded 64-token-per-rank slice, checked on
+    the host against oracle/ (the checker only; outside every timed region):
+    the dispatched x and dy rows bit-exact against ep_oracle.simulate; the
+    quantised GEMM operands bit-exact against the oracle quantiser; sampled
+    entries of every GEMM output (gate/up, down, both dgrads, both wgrads)
+    against fp64 products of the dequantised operands (relative Frobenius
+    <= 1e-3 against the product rounded to the output dtype); SwiGLU's
+    encoded h against fp64 silu(g)*u (<= 6e-2, MXFP8 rounding); the combined
+    output and input gradient against the oracle's combine of every rank's
+    rows (one bf16 ulp plus 2^-20 of the sum of magnitudes).  Every rank
+    checks its own share; the flags are reduced over the group."""
+    from oracle import ep_oracle
+    from oracle import mxfp8_oracle as orc
+    m = pkg()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    E, k, n = lb.num_experts, EP_TOPK, VERIFY_TOKENS
+    W = m.workloads
+    xs, dys, ids, ps = [], [], [], []
+    for r in range(world):                  # every rank's slice, identically on every rank
+        g = np.random.default_rng(seed * 1009 + 77 + r)
+        ids.append(W.zipf_topk_sample(n, lb.logp, k, seed=seed * 7919 + 501 + r))
+        xs.append(_bf16_np(g.standard_normal((n, HIDDEN)))[1])
+        dys.append(_bf16_np(g.standard_normal((n, HIDDEN)) * 1e-2)[1])
+        p = g.random((n, k)) + 0.1
+        ps.append((p / p.sum(1, keepdims=True)).astype(np.float32))
+    layer = lb.layer
+    layer.trace = {}
+    res = layer.step(_bf16_np(xs[rank])[0].to(dev), torch.from_numpy(ids[rank]).to(dev),
+                     torch.from_numpy(ps[rank]).to(dev), _bf16_np(dys[rank])[0].to(dev))
+    torch.cuda.synchronize()
+    tr, layer.trace = layer.trace, None
+    checks = {"device_error": m.device_error() == 0}
+    sim, routed, sc = ep_oracle.simulate(xs, ids, E, slot_of_expert=lb.slot)
+    sim_dy = ep_oracle.simulate(dys, ids, E, slot_of_expert=lb.slot)[0]
+    x_local = tr["x_local"].float().cpu().numpy().astype(np.float64)
+    dy_local = tr["dy_local"].float().cpu().numpy().astype(np.float64)
+    checks["dispatch_x_bit_exact"] = bool(np.array_equal(x_local, sim[rank][0]))
+    checks["dispatch_dy_bit_exact"] = bool(np.array_equal(dy_local, sim_dy[rank][0]))
+    # real rows of each local expert group (the rest is zero padding)
+    real = sim[rank][1].sum(0)
+    gstart = np.concatenate([[0], np.cumsum(sim[rank][2]["group_rows"])])
+    rows = np.concatenate([np.arange(gstart[e], gstart[e] + real[e]) for e in range(real.size)])
+    expert_of = np.searchsorted(gstart, rows, side="right") - 1
+    bits = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)
+    u8 = lambda t: t.view(torch.uint8).cpu().numpy()
+    xb, dyb = bits(tr["x_local"]), bits(tr["dy_local"])
+    q, s_ = orc.quantize_rowwise(xb)
+    qt, st = orc.quantize_colwise(xb)
+    checks["quantize_x_bit_exact"] = bool(np.array_equal(q, u8(tr["xq"])) and np.array_equal(s_, u8(tr["xs"]))
+                                          and np.array_equal(qt, u8(tr["ia_g"]))
+                                          and np.array_equal(st, u8(tr["ias_g"])))
+    q, s_ = orc.quantize_rowwise(dyb)
+    qt, st = orc.quantize_colwise(dyb)
+    checks["quantize_dy_bit_exact"] = bool(np.array_equal(q, u8(tr["dyq"])) and np.array_equal(s_, u8(tr["dys"]))
+                                           and np.array_equal(qt, u8(tr["go_d"]))
+                                           and np.array_equal(st, u8(tr["gos_d"])))
+    rng = np.random.default_rng(seed + 4242 + rank)
+    errs = {}
+
+    def fwd_check(name, a, w, out):
+        """Sampled (row, column) entries of out = deq(a) . deq(w[expert])^T."""
+        aq, as_ = a
+        wq, ws = w
+        N = wq.shape[1]
+        ri = rng.integers(0, rows.size, VERIFY_SAMPLES)
+        r, e = rows[ri], expert_of[ri]
+        c = rng.integers(0, N, VERIFY_SAMPLES)
+        rt, et, ct = (torch.from_numpy(v).to(dev) for v in (r, e, c))
+        A = orc.dequantize(u8(aq[rt]), u8(as_[rt]))
+        Wr = orc.dequantize(u8(wq[et, ct]), u8(ws[et, ct]))
+        ref = orc.round_to_bf16((A * Wr).sum(1))
+        got = out[rt, ct].float().cpu().numpy().astype(np.float64)
+        errs[name] = orc.rel_frobenius(got, ref)
+
+    def wgrad_check(name, go, ia, dw):
+        """Sampled (expert, row, column) entries of dW[e] = deq(go)[:, tokens
+        of e] . deq(ia)[:, tokens of e]^T (the group's padded range: padding
+        tokens are zero)."""
+        goq, gos = go
+        iaq, ias = ia
+        Ee, N, K = dw.shape
+        e = rng.integers(0, Ee, VERIFY_SAMPLES)
+        nn, kk = rng.integers(0, N, VERIFY_SAMPLES), rng.integers(0, K, VERIFY_SAMPLES)
+        G = orc.dequantize(u8(goq[torch.from_numpy(nn).to(dev)]), u8(gos[torch.from_numpy(nn).to(dev)]))
+        I_ = orc.dequantize(u8(iaq[torch.from_numpy(kk).to(dev)]), u8(ias[torch.from_numpy(kk).to(dev)]))
+        ref = np.array([(G[i, gstart[e[i]]:gstart[e[i] + 1]] * I_[i, gstart[e[i]]:gstart[e[i] + 1]]).sum()
+                        for i in range(VERIFY_SAMPLES)])
+        if dw.dtype == torch.bfloat16:
+            ref = orc.round_to_bf16(ref)
+        got = dw[torch.from_numpy(e).to(dev), torch.from_numpy(nn).to(dev),
+                 torch.from_numpy(kk).to(dev)].float().cpu().numpy().astype(np.float64)
+        errs[name] = orc.rel_frobenius(got, ref)
+
+    fwd_check("fwd_gate_up", (tr["xq"], tr["xs"]), layer.wgu, tr["gu"])
+    fwd_check("fwd_down", (tr["hq"], tr["hs"]), layer.wd, tr["y_local"])
+    fwd_check("dgrad_down", (tr["dyq"], tr["dys"]), layer.wdt, tr["dh"])
+    if layer.compute_dx:
+        fwd_check("dgrad_gate_up", (tr["dgq"], tr["dgs"]), layer.wgut, tr["dx_local"])
+    wgrad_check("wgrad_down", (tr["go_d"], tr["gos_d"]), (tr["ia_d"], tr["ias_d"]), res.dw_down)
+    wgrad_check("wgrad_gate_up", (tr["go_g"], tr["gos_g"]), (tr["ia_g"], tr["ias_g"]), res.dw_gate_up)
+    # SwiGLU: the encoded h against fp64 silu(g) * u on the real rows
+    gu = tr["gu"][torch.from_numpy(rows).to(dev)].float().cpu().numpy().astype(np.float64)
+    g_, u_ = gu[:, :INTER], gu[:, INTER:]
+    h = g_ / (1.0 + np.exp(-g_)) * u_
+    rt = torch.from_numpy(rows).to(dev)
+    errs["swiglu_h_mxfp8"] = orc.rel_frobenius(orc.dequantize(u8(tr["hq"][rt]), u8(tr["hs"][rt])), h)
+    checks["gemms_within_1e-3"] = all(v <= 1e-3 for kname, v in errs.items() if kname != "swiglu_h_mxfp8")
+    checks["swiglu_within_6e-2"] = errs["swiglu_h_mxfp8"] <= 6e-2
+
+    # combine: every rank's expert outputs, gathered, through the oracle's
+    # inverse exchange and weighted sum
+    def all_rows(t):
+        if world == 1:
+            return [t.float().cpu().numpy()]
+        sz = torch.tensor([t.shape[0]], device=dev)
+        sizes = [torch.empty_like(sz) for _ in range(world)]
+        torch.distributed.all_gather(sizes, sz)
+        mx = int(max(v.item() for v in sizes))
+        pad = torch.zeros(mx, t.shape[1], dtype=t.dtype, device=dev)
+        pad[:t.shape[0]] = t
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        torch.distributed.all_gather(parts, pad)
+        return [p[:int(v.item())].float().cpu().numpy() for p, v in zip(parts, sizes)]
+
+    def combine_ok(got, ys, weights):
+        """got within one bf16 ulp of the oracle's fp32 weighted sum, plus
+        the fp32 rounding of the k-term sum relative to the sum of magnitudes."""
+        plans = [o[2] for o in sim]
+        want = ep_oracle.simulate_combine(ys, routed, sc, plans, weights, [n] * world, k)[rank]
+        mag = ep_oracle.simulate_combine([np.abs(y) for y in ys], routed, sc, plans,
+                                         [None if w is None else np.abs(w) for w in weights],
+                                         [n] * world, k)[rank]
+        g = got.float().cpu().numpy()
+        return bool(np.all(np.abs(g - want) <= np.abs(want) * 2.0 ** -7 + mag * 2.0 ** -20))
+
+    checks["combine_out"] = combine_ok(res.out, all_rows(tr["y_local"]), ps)
+    if layer.compute_dx:
+        checks["combine_dx"] = combine_ok(res.dx, all_rows(tr["dx_local"]), [None] * world)
+    ok = all(checks.values())
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+    return {"ok": bool(flag.item()), "transport": lb.ep.transport, "tokens_per_rank": n,
+            "rank0_checks": checks, "rank0_rel_err": {kk: float(f"{v:.3g}") for kk, v in errs.items()}}
+
+
 def run_ep_mxg(args, rank, world, local):
-    """The N>1 bench line: config 4 across the process group."""
+    """The N>1 bench line: config 4 across the process group, the NVLink
+    peer-memory transport timed, then the NCCL all-to-all transport; each
+    verified on a seeded slice outside its timed region."""
     pkg()._lib.load()
     lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
                       transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
-                      wgrad_dtype=args.ep_wgrad_dtype)
+                      wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -700,30 +970,102 @@ def run_ep_mxg(args, rank, world, local):
         e_ms = max_over_ranks(e_ms, world)
         e2e = {"value": round(r["flops_per_step_all_ranks"] / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3)}
+    verified = {lb.ep.transport: verify_ep_layer(lb, world, rank, args.seed)}
+    lb.close()
+    del lb
+    torch.cuda.empty_cache()
+    other = None
+    if args.transport != "nccl" and not args.no_nccl_layer:
+        lb2 = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=False,
+                           transport="nccl", wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx)
+        r2 = measure_ep_layer(lb2, world, min(args.steps, 20), args.warmup)
+        verified["nccl"] = verify_ep_layer(lb2, world, rank, args.seed)
+        other = {"transport": "nccl", "value": round(r2["value"], 2), "unit": "TFLOPS",
+                 "ms_per_step": round(r2["ms_per_step"], 4), "steps": min(args.steps, 20),
+                 "segments_ms_rank0": r2["segments_ms_rank0"], "exchange_ms_rank0": r2["exchange_ms_rank0"],
+                 "gemm_tflops_rank0": r2["gemm_tflops_rank0"],
+                 "gpu_launches_per_step": EP_LAUNCHES_PER_STEP["nccl"]}
+        lb2.close()
+        del lb2
+        torch.cuda.empty_cache()
+    ok = all(v["ok"] for v in verified.values())
     out = {"metric": METRIC, "value": round(r["value"], 2), "unit": "TFLOPS", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
            "data": "synthetic",
-           "config": {"workload": "dsv3_ep_layer (config 4): dispatch, quantize, gate/up fwd, swiglu, "
-                                  "down fwd, combine + down dgrad and both wgrads",
-                      "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
-                      "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
-                      "hidden": HIDDEN, "intermediate": INTER, "placement": r["placement"],
-                      "comm_overlap": r["overlap"], "transport": r["transport"],
-                      "reserved_sms": r["reserve_sms"],
-                      "dw_dtype": lb.wgrad_dtype + (" (the reference's wgrad output dtype)"
-                                                    if lb.wgrad_dtype == "bf16" else ""),
-                      "parallelism": f"ep{world}",
-                      "l2": "operands > L2 (no flush needed)"},
+           "config": ep_config(world, args.placement, args.overlap, r["transport"], r["reserve_sms"],
+                               args.ep_wgrad_dtype, args.seed, not args.no_dx),
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
-               "padded_rows_this_rank", "segments_ms_rank0", "gemm_tflops_rank0")},
+               "padded_rows_this_rank", "segments_ms_rank0", "exchange_ms_rank0", "gemm_ms_rank0",
+               "gemm_tflops_rank0")},
+           "layer_nccl": other, "verified": verified,
            "cpu_baseline": None, "e2e": e2e,
            "gpu_launches": args.steps * EP_LAUNCHES_PER_STEP[r["transport"]], "clocks": clk.summary()}
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if not ok:
+        raise SystemExit("expert-parallel layer verification failed: " + json.dumps(verified))
+
+
+def ep_routing_stats(world, seed, placement):
+    """Rows every rank receives at config 4 (its tokens' routing replayed on
+    the host with the bench's seeds): (rows per rank, padded rows of rank 0)."""
+    m = pkg()
+    W = m.workloads
+    logp = W.zipf_log_popularity(EP_EXPERTS, EP_ZIPF, seed)
+    slot = np.arange(EP_EXPERTS)
+    if placement == "balanced" and world > 1:
+        slot = m.ep.balanced_placement(W.expected_expert_load(logp, EP_TOPK), world)
+    per_slot = np.zeros(EP_EXPERTS, np.int64)
+    for r in range(world):
+        ids = W.zipf_topk_sample(EP_TOKENS, logp, EP_TOPK, seed=seed * 7919 + 1 + r)
+        per_slot += np.bincount(slot[ids.reshape(-1)], minlength=EP_EXPERTS)
+    el = EP_EXPERTS // world
+    rows = per_slot.reshape(world, el).sum(1)
+    padded0 = int(((per_slot[:el] + 31) // 32 * 32).sum())
+    return rows, padded0
+
+
+def ep_flops(rows, dx=True):
+    """GEMM FLOPs of one config-4 layer step on `rows` received rows."""
+    return (18 if dx else 14) * int(rows) * HIDDEN * INTER
+
+
+def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx):
+    """The config object of a config-4 line (the reference arm prints the same)."""
+    rows, padded = ep_routing_stats(world, seed, placement)
+    flops_rank = ep_flops(rows[0], dx)
+    rows_max = int(rows.max())
+    return {"workload": "dsv3_ep_layer (config 4): dispatch, quantize, gate/up fwd, swiglu, down fwd, "
+                        "combine + down dgrad, swiglu bwd" + (", gate/up dgrad (dx) and its return" if dx else "")
+                        + " and both wgrads",
+            "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
+            "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
+            "hidden": HIDDEN, "intermediate": INTER, "placement": placement,
+            "comm_overlap": overlap, "transport": transport, "reserved_sms": reserve_sms,
+            "dw_dtype": wgrad_dtype + (" (the reference's wgrad output dtype)" if wgrad_dtype == "bf16" else ""),
+            "routed_rows_per_gpu": EP_TOKENS * EP_TOPK, "max_rows_received_per_gpu": rows_max,
+            "padded_rows": padded,  # rank 0's
+            "routing": f"top-{EP_TOPK} of {EP_EXPERTS} experts by Zipf({EP_ZIPF}) popularity, "
+                       f"{placement} placement, groups padded to 32",
+            "flops_per_step_per_gpu": flops_rank, "parallelism": f"ep{world}",
+            "l2": "operands > L2 (no flush needed)"}
+
 
 # ---------------------------------------------------------------- arms
+def gemm_config(split, case="dsv3"):
+    """The config object of the N=1 line (the reference arm prints the same)."""
+    flops = 2 * split.real_rows * (GATE_UP * HIDDEN + HIDDEN * INTER + GATE_UP * HIDDEN)
+    return {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)"
+            if case == "dsv3" else "small profiling case (8 experts, 16384 rows)",
+            "experts_per_gpu": split.E, "hidden": HIDDEN, "intermediate": INTER,
+            "routed_rows_per_gpu": split.real_rows, "padded_rows": split.M,
+            "routing": "multinomial over Dirichlet(1.0), groups padded to 32",
+            "flops_per_step_per_gpu": flops, "l2": "operands > L2 (no flush needed)",
+            "parallelism": "single"}
+
+
 def traffic_from_profiles():
     path = os.path.join(REPO, "profiles", "ncu_traffic.json")
     if os.path.exists(path):
@@ -761,12 +1103,10 @@ def run_mxg(args, rank, world, local):
     dom = max(run_ms, key=lambda k: run_ms[k])
     traffic = traffic_from_profiles().get(dom)
     achieved = wl.flops[dom] / (run_ms[dom] * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": f"grouped_gemm_kernel ({dom})",
-                "achieved": round(achieved, 1), "peak": round(pk["fp8_tflops"], 1),
-                "unit": "TFLOP/s", "frac": round(achieved / pk["fp8_tflops"], 4),
-                "frac_of_burst_peak": round(achieved / pk["fp8_tflops_burst"], 4),
-                "peak_source": pk["source"], "traffic": traffic,
-                "flops_per_launch": wl.flops[dom], "per_kernel": per}
+    roofline = tensor_roofline(achieved, ms_step * args.steps * 1e-3, pk,
+                               kernel=f"grouped_gemm_kernel ({dom})", traffic=traffic,
+                               flops_per_launch=wl.flops[dom], kernel_ms=round(run_ms[dom], 4),
+                               per_kernel=per)
     # quantiser throughput (separate timed loop, HBM bound)
     torch.cuda.synchronize()
     qs, qe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -803,13 +1143,7 @@ def run_mxg(args, rank, world, local):
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
            "data": "synthetic",
-           "config": {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)"
-                      if args.case == "dsv3" else "small profiling case (8 experts, 16384 rows)",
-                      "experts_per_gpu": wl.E, "hidden": HIDDEN, "intermediate": INTER,
-                      "routed_rows_per_gpu": wl.split.real_rows, "padded_rows": wl.M,
-                      "routing": "multinomial over Dirichlet(1.0), groups padded to 32",
-                      "flops_per_step_per_gpu": flops_step, "l2": "operands > L2 (no flush needed)",
-                      "parallelism": f"ep{world}" if world > 1 else "single"},
+           "config": gemm_config(wl.split, args.case),
            "roofline": roofline, "quantize": quant, "cpu_baseline": cpu, "e2e": e2e,
            "gpu_launches": args.steps * sum(LAUNCHES_PER_CALL.values()),
            "clocks": clk.summary()}
@@ -821,18 +1155,33 @@ def run_mxg(args, rank, world, local):
     if not args.no_ep and args.case == "dsv3":
         del wl, calls
         torch.cuda.empty_cache()
+        # the weak-scaling base: one GPU carrying a rank's load of the 8-GPU
+        # config-4 run (rank 0's 32 experts, 16384 tokens top-8), the
+        # exchanges degenerating to local gathers
         lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=False,
-                          wgrad_dtype=args.ep_wgrad_dtype)
-        r = measure_ep_layer(lb, world, min(args.steps, 50), args.warmup)
+                          wgrad_dtype=args.ep_wgrad_dtype, experts=32, logp=rank0_like_popularity(args.seed),
+                          compute_dx=not args.no_dx)
+        steps = min(args.steps, 50)
+        r = measure_ep_layer(lb, world, steps, args.warmup)
+        verified = verify_ep_layer(lb, world, rank, args.seed)
+        lb.close()
         del lb
+        torch.cuda.empty_cache()
         out["ep_layer_1gpu"] = {"value": round(r["value"], 2), "unit": "TFLOPS",
-                                "ms_per_step": round(r["ms_per_step"], 4),
-                                "note": "config 4 layer on one GPU (all 256 experts, 16384 tokens): "
-                                        "the same per-GPU work as each rank of the N>1 lines",
-                                "dw_dtype": args.ep_wgrad_dtype,
-                                "gemm_tflops": r["gemm_tflops_rank0"],
+                                "ms_per_step": round(r["ms_per_step"], 4), "steps": steps,
+                                "note": "weak-scaling base of the config-4 lines: one GPU with the load of a "
+                                        "rank of the 8-GPU run (rank 0's 32 experts under balanced placement, "
+                                        "16384 tokens top-8, ~131072 routed rows; exchanges are local gathers)",
+                                "dw_dtype": args.ep_wgrad_dtype, "dx": not args.no_dx,
+                                "gemm_tflops": r["gemm_tflops_rank0"], "gemm_ms": r["gemm_ms_rank0"],
                                 "segments_ms": r["segments_ms_rank0"],
-                                "recv_rows": r["recv_rows_per_rank"]["max"]}
+                                "recv_rows": r["recv_rows_per_rank"]["max"],
+                                "padded_rows": r["padded_rows_this_rank"],
+                                "flops_per_step": r["flops_per_step_this_rank"],
+                                "roofline": r["roofline"], "verified": verified}
+        if not verified["ok"]:
+            print(json.dumps(out), flush=True)
+            raise SystemExit("one-GPU expert layer verification failed")
     if rank == 0:
         print(json.dumps(out), flush=True)
 
@@ -853,8 +1202,10 @@ def cpu_reference_layer_sample(host, threads):
         dy = deq(e["dyq"], e["dys"])
         _ = dy @ deq(e["wdt"], e["wdts"]).T                   # down dgrad   [r, 2048]
         _ = deq(e["go_d"], e["gos_d"]) @ deq(e["ia_d"], e["ias_d"]).T   # down wgrad
+        if "dgq" in e:
+            _ = deq(e["dgq"], e["dgs"]) @ deq(e["wgut"], e["wguts"]).T  # gate/up dgrad [r, 7168]
         _ = deq(e["go_g"], e["gos_g"]) @ deq(e["ia_g"], e["ias_g"]).T   # gate/up wgrad
-        flops += 14 * r * HIDDEN * INTER
+        flops += ep_flops(r, "dgq" in e)
     return flops, time.perf_counter() - t0
 
 
@@ -883,6 +1234,9 @@ def run_reference_layer(args, world):
                      "ia_d": rnd(INTER, r), "ias_d": sc(INTER, r // 32),
                      "go_g": rnd(GATE_UP, r), "gos_g": sc(GATE_UP, r // 32),
                      "ia_g": rnd(HIDDEN, r), "ias_g": sc(HIDDEN, r // 32)})
+        if not args.no_dx:
+            host[-1].update(dgq=rnd(r, GATE_UP), dgs=sc(r, GATE_UP // 32),
+                            wgut=rnd(HIDDEN, GATE_UP), wguts=sc(HIDDEN, GATE_UP // 32))
     for _ in range(args.warmup):
         cpu_reference_layer_sample(host, threads)
     tot_fl, tot_dt = 0, 0.0
@@ -892,16 +1246,17 @@ def run_reference_layer(args, world):
         tot_dt += dt
     v = tot_fl / tot_dt / 1e12
     sample = (f"per step experts {experts} ({[h['rows'] for h in host]} rows) of the config-4 layer: "
-              "gate/up fwd, down fwd, down dgrad, both wgrads; torch fp32 dequantise+matmul "
+              "gate/up fwd, down fwd, down dgrad, " + ("gate/up dgrad, " if not args.no_dx else "") +
+              "both wgrads; torch fp32 dequantise+matmul "
               "(reference fused_fwd.py:249-264, scale_correctness.py:110-137); no all-to-all (one host)")
     out = {"metric": METRIC, "value": round(v, 4), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(1e3 * tot_dt / args.steps, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": "synthetic", "impl": "reference",
-           "config": {"workload": "dsv3_ep_layer (config 4) GEMMs, CPU sample",
-                      "experts": EP_EXPERTS, "experts_per_gpu": EP_EXPERTS // world,
-                      "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "hidden": HIDDEN,
-                      "intermediate": INTER, "parallelism": f"ep{world}"},
+           "config": ep_config(world, args.placement, args.overlap,
+                               "nccl" if args.transport == "nccl" else "p2p",
+                               args.reserve_sms if args.overlap else 0, args.ep_wgrad_dtype, args.seed,
+                               not args.no_dx),
            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
                             "kind": "port", "sample": sample},
            "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -949,8 +1304,7 @@ def run_reference(args, rank, world, local):
            "warmup": args.warmup, "ms_per_step": round(1e3 * tot_dt / args.steps, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": "synthetic", "impl": "reference",
-           "config": {"workload": "dsv3_gemms: fwd gate/up (cfg1) + wgrad down + wgrad gate/up (cfg2)",
-                      "experts_per_gpu": E, "hidden": HIDDEN, "intermediate": INTER},
+           "config": gemm_config(sp),
            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
                             "kind": "port",
                             "sample": f"per step experts {experts} (their fwd gate/up + both wgrads), "
@@ -984,10 +1338,19 @@ def main():
     ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
                     help="weight-gradient dtype of the config-4 expert layer (bf16: the reference's "
                          "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
+    ap.add_argument("--no-dx", action="store_true",
+                    help="EP layer: skip the gate/up dgrad (input gradient) and its return")
+    ap.add_argument("--no-nccl-layer", action="store_true",
+                    help="N>1: skip the second measurement of the layer over NCCL all-to-all")
+    ap.add_argument("--fp8-peak", action="store_true",
+                    help="measure cuBLAS MXFP8 (torch._scaled_mm) burst and sustained throughput and exit")
     ap.add_argument("--reserve-sms", type=int, default=0,
                     help="EP layer with --overlap: SMs kept free of GEMM blocks for the peer copies")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.fp8_peak:
+        measure_fp8_peak(args)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")), 0)

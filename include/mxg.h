@@ -70,7 +70,10 @@ MXG_API const char* mxg_error_string(int code);
 MXG_API int mxg_version(void);
 
 /* Read (and optionally clear) the current device's error word.  Synchronises
- * the device.  *code receives 0 or the first MXG_ERR_* a kernel recorded. */
+ * the device.  *code receives 0 or the first MXG_ERR_* a kernel recorded.
+ * The library looks up each device's error word once and keeps the address
+ * for the life of the process, so cudaDeviceReset() on a device it has used
+ * is not supported. */
 MXG_API int mxg_get_device_error(int* code, int clear);
 
 /* ---- MXFP8 quantisers (RCEIL E8M0 scales, RNE e4m3, saturating) ------------
@@ -126,7 +129,9 @@ MXG_API int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups, in
  * a device share the one array: calls that overlap on the GPU (different
  * streams, or different host threads) race; run them in order on one stream.
  * Nothing in the array needs to start zeroed: each call rewrites what it reads.
- * It calls no cudaMalloc/cudaFree. */
+ * It calls no cudaMalloc/cudaFree.  The looked-up address (like the error
+ * word's) is kept for the life of the process: cudaDeviceReset() on a device
+ * this library has used is not supported. */
 #define MXG_NOALLOC_SCRATCH_BYTES (64u << 20)
 MXG_API int mxg_grouped_fwd_noalloc(const void* a, const void* a_scales, const void* w,
                                     const void* w_scales, const int32_t* offs, int offs_len,
@@ -259,15 +264,19 @@ MXG_API int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slots,
 /* Row src[send_rows[p]] -> row dest_base[s] + p of peer_bufs[s / e_local]
  * (peer_bufs: device array of every rank's buffer address), starting with
  * the positions bound for rank me+1 so that the ranks write to different
- * peers at the same time.  A destination row outside [0, capacity_rows) is
- * skipped and sets the device error word.  max_blocks <= 0: the library's
+ * peers at the same time.  Only the positions p < slot_start[num_slots] are
+ * sent (routing slots with an out-of-range expert id are counted nowhere).
+ * A destination row outside [0, capacity_rows) or a source row outside
+ * [0, src_rows) is skipped and sets the device error word
+ * (MXG_ERR_WORKSPACE_TOO_SMALL, MXG_ERR_INVALID_ARGUMENT).  max_blocks <= 0: the library's
  * default grid, sharing SMs with concurrent work; max_blocks > 0: that many
  * 1024-thread blocks that only run on SMs no GEMM block occupies (pair with
  * mxg_set_gemm_sm_limit to overlap an exchange with the GEMMs). */
-MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
-                                int64_t n_send, const int32_t* slot_start, const int32_t* dest_base,
-                                int num_slots, int e_local, int me, const uint64_t* peer_bufs,
-                                int64_t capacity_rows, int max_blocks, void* stream);
+MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t src_rows, int64_t row_bytes,
+                                const int32_t* send_rows, int64_t n_send, const int32_t* slot_start,
+                                const int32_t* dest_base, int num_slots, int e_local, int me,
+                                const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
+                                void* stream);
 
 /* Padded local rows q = ret_order[i] (i < n_rows) -> row back_row[q] of
  * peer_bufs[back_rank[q]] (skipped where back_rank < 0). */

@@ -149,34 +149,44 @@ __device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uin
 // -> row dest_base[s] + p of rank s / e_local.  One warp per row.  Send
 // positions are ordered by destination rank; every rank starts with the
 // positions of the rank after it (rotation `rot`), so at any moment the ranks
-// write to different peers instead of all to the same one.
+// write to different peers instead of all to the same one.  Only positions
+// below slot_start[E] are routed (a routing slot whose expert id was out of
+// range is counted nowhere and leaves its send_rows entry unwritten), and a
+// source row outside [0, src_rows) is skipped and reported.
 __global__ void __launch_bounds__(kCopyThreadsExclusive) p2p_dispatch_kernel(
-    const uint4* __restrict__ src, int64_t row_vecs, const int32_t* __restrict__ send_rows,
-    int64_t n_send, const int32_t* __restrict__ slot_start, const int32_t* __restrict__ dest_base,
-    int E, int e_local, int me, const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows,
-    int* err) {
+    const uint4* __restrict__ src, int64_t src_rows, int64_t row_vecs,
+    const int32_t* __restrict__ send_rows, int64_t n_send, const int32_t* __restrict__ slot_start,
+    const int32_t* __restrict__ dest_base, int E, int e_local, int me,
+    const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows, int* err) {
   __shared__ int32_t ss[kMaxSlotsSmem];
   for (int i = threadIdx.x; i <= E; i += blockDim.x) ss[i] = slot_start[i];
   __syncthreads();
   const int world = E / e_local;
-  const int64_t rot = ss[((me + 1) % world) * e_local];
+  const int64_t n_valid = min(n_send, int64_t(ss[E]));
+  if (n_valid <= 0) return;
+  const int64_t rot = min(int64_t(ss[((me + 1) % world) * e_local]), n_valid);
   const int lane = threadIdx.x & 31;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t i = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n_send;
+  for (int64_t i = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n_valid;
        i += warps) {
-    const int64_t p = (i + rot) % n_send;
+    const int64_t p = (i + rot) % n_valid;
     int lo = 0, hi = E - 1;  // last slot with ss[s] <= p
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (ss[mid] <= p) lo = mid; else hi = mid - 1;
     }
     const int64_t row = int64_t(dest_base[lo]) + p;
+    const int64_t src_row = send_rows[p];
     if (row < 0 || row >= capacity_rows) {
       if (lane == 0) atomicCAS(err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
       continue;
     }
+    if (src_row < 0 || src_row >= src_rows) {
+      if (lane == 0) atomicCAS(err, 0, MXG_ERR_INVALID_ARGUMENT);
+      continue;
+    }
     warp_copy_row(reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs,
-                  src + int64_t(send_rows[p]) * row_vecs, row_vecs, lane);
+                  src + src_row * row_vecs, row_vecs, lane);
   }
   __threadfence_system();
 }
@@ -322,12 +332,12 @@ extern "C" int mxg_ep_p2p_plan(const int32_t* counts_all, int world, int num_slo
   return cuda_status(cudaGetLastError());
 }
 
-extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int32_t* send_rows,
-                                   int64_t n_send, const int32_t* slot_start,
-                                   const int32_t* dest_base, int num_slots, int e_local, int me,
-                                   const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
-                                   void* stream) {
-  if (n_send < 0 || row_bytes < 0 || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
+extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t src_rows, int64_t row_bytes,
+                                   const int32_t* send_rows, int64_t n_send,
+                                   const int32_t* slot_start, const int32_t* dest_base,
+                                   int num_slots, int e_local, int me, const uint64_t* peer_bufs,
+                                   int64_t capacity_rows, int max_blocks, void* stream) {
+  if (n_send < 0 || src_rows < 0 || row_bytes < 0 || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
       e_local < 1 || num_slots % e_local != 0 || capacity_rows < 0 || me < 0 ||
       me >= num_slots / e_local)
     return MXG_ERR_INVALID_ARGUMENT;
@@ -342,8 +352,8 @@ extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t row_bytes, const int
   const CopyLaunch cl = copy_launch(n_send, max_blocks);
   if (cl.smem && (st = allow_exclusive_smem(p2p_dispatch_kernel))) return st;
   p2p_dispatch_kernel<<<cl.blocks, cl.threads, cl.smem, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint4*>(src), row_bytes / 16, send_rows, n_send, slot_start, dest_base,
-      num_slots, e_local, me, peer_bufs, capacity_rows, err);
+      reinterpret_cast<const uint4*>(src), src_rows, row_bytes / 16, send_rows, n_send, slot_start,
+      dest_base, num_slots, e_local, me, peer_bufs, capacity_rows, err);
   return cuda_status(cudaGetLastError());
 }
 

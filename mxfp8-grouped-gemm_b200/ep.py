@@ -118,8 +118,8 @@ class CudaP2POps:
                  max_blocks=0):
         src = src.contiguous()
         row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
-        _lib.check(self.L.mxg_ep_dispatch_p2p(src.data_ptr() if src.numel() else None, row_bytes,
-                                              send_rows.data_ptr(), send_rows.numel(),
+        _lib.check(self.L.mxg_ep_dispatch_p2p(src.data_ptr() if src.numel() else None, src.shape[0],
+                                              row_bytes, send_rows.data_ptr(), send_rows.numel(),
                                               slot_start.data_ptr(), dest_base.data_ptr(),
                                               dest_base.numel(), e_local, me, peer_ptrs.data_ptr(),
                                               capacity_rows, max_blocks,
@@ -347,6 +347,12 @@ class ExpertParallel:
         self.buffers[name] = PeerBuffer(max(rows, 1) * row_bytes, self.group, self.world, self.rank, device)
         self.capacity[name] = (max(rows, 1), row_bytes)
 
+    def _ensure_ret(self, name, device):
+        need, alloc, row_bytes = self._ret_need
+        rows, rb = self.capacity.get(name, (0, 0))
+        if rows < need or rb != row_bytes:
+            self._ensure_buffer(name, alloc, row_bytes, device)
+
     def local_experts(self) -> list:
         """Global expert id held in each local slot of this rank."""
         lo = self.rank * self.e_local
@@ -391,10 +397,21 @@ class ExpertParallel:
 
     def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos):
         E, W, El, pad = self.num_experts, self.world, self.e_local, self.pad
-        C = torch.empty(W * E, dtype=torch.int32, device=x.device)
-        dist.all_gather_into_tensor(C, counts, group=self.group)   # also: every receiver is idle
-        C = C.view(W, E)
-        Ch = C.cpu().numpy().astype(np.int64)
+        # every rank's slot counts plus its number of routing slots n*k: a
+        # routing slot whose expert id is out of range is counted nowhere, and
+        # every rank sees that from the same gathered table and raises before
+        # any peer store
+        mine = torch.cat([counts, torch.full((1,), n * k, dtype=torch.int32, device=x.device)])
+        Cx = torch.empty(W * (E + 1), dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(Cx, mine, group=self.group)   # also: every receiver is idle
+        Cx = Cx.view(W, E + 1)
+        Chx = Cx.cpu().numpy().astype(np.int64)
+        Ch = Chx[:, :E]
+        bad = np.nonzero(Ch.sum(1) != Chx[:, E])[0]
+        if bad.size:
+            lost = ", ".join(f"rank {r}: {int(Chx[r, E] - Ch[r].sum())}" for r in bad)
+            raise ValueError(f"expert ids outside [0, {E}): routing slots counted nowhere ({lost})")
+        C = Cx[:, :E].contiguous()
         tot = Ch.sum(0).reshape(W, El)                             # rows per (owner, local slot)
         padded = (tot + pad - 1) // pad * pad
         m_pad_all = padded.sum(1)
@@ -409,9 +426,12 @@ class ExpertParallel:
             rows, rb = self.capacity.get(name, (0, 0))
             if rows < need or rb != row_bytes:
                 self._ensure_buffer(name, max(worst, need), row_bytes, x.device)
-        rows, rb = self.capacity.get("ret", (0, 0))
-        if rows < int(sent.max()) or rb != row_bytes:
-            self._ensure_buffer("ret", max(n_cap * k, int(sent.max())), row_bytes, x.device)
+        # return buffers ("ret", and any other combine_send names): every
+        # rank's n*k rows in send order; sized like the receive buffers, from
+        # the gathered counts, so every rank (re)allocates them together
+        self._ret_need = (int(sent.max()), max(n_cap * k, int(sent.max())), row_bytes)
+        for name in [b for b in self.capacity if b not in ("x", "dy")] or ["ret"]:
+            self._ensure_ret(name, x.device)
         slot_start, dest_base, group_rows, _, back_rank, back_row, ret_order = self.p2p.plan(
             C, self.rank, pad, m_pad, recv_rows)
         send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
@@ -430,6 +450,9 @@ class ExpertParallel:
             buf = self.buffers[buffer]
             rows, row_bytes = self.capacity[buffer]
             if x.shape[0] and x.element_size() * x[0].numel() != row_bytes:
+                # still take part in the closing rendezvous, so the other
+                # ranks are not left waiting in it, then fail
+                self._barrier(x.device)
                 raise ValueError("row size differs from the receive buffer's")
             local = buf.view(m_pad, x)
             self.p2p.zero_pad_rows(local, plan.back_rank)
@@ -446,14 +469,19 @@ class ExpertParallel:
         sum over each token's choices (weighted when weights [n, k] given)."""
         return self.combine_finish(self.combine_send(y_local, plan), plan, weights)
 
-    def combine_send(self, y_local: torch.Tensor, plan: DispatchPlan) -> torch.Tensor:
+    def combine_send(self, y_local: torch.Tensor, plan: DispatchPlan, buffer: str = "ret") -> torch.Tensor:
         """First half of ``combine``: every result row back to its home rank.
         Returns this rank's rows in send order [n*k, H'] (with the p2p
-        transport: a view of the "ret" buffer, valid until the next combine)."""
+        transport: a view of the named return buffer, valid until the next
+        combine into it; every rank must use the same buffer names in the
+        same order, since a first use allocates collectively)."""
         if plan.back_rank is not None:
-            buf = self.buffers["ret"]
-            rows, row_bytes = self.capacity["ret"]
+            if buffer not in self.buffers:
+                self._ensure_ret(buffer, y_local.device)
+            buf = self.buffers[buffer]
+            rows, row_bytes = self.capacity[buffer]
             if y_local.shape[0] and y_local.element_size() * y_local[0].numel() != row_bytes:
+                self._barrier(y_local.device)   # as in dispatch_like: nobody waits for this rank
                 raise ValueError("combine rows must have the dispatched rows' size")
             self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
                          self.p2p_max_blocks)

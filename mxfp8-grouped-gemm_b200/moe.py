@@ -1,33 +1,47 @@
 """MoE expert FFN over expert parallelism on the MXFP8 grouped GEMMs.
 
 The layer the reference trains with (``e2e_bench.py:56-61,91-108``: gate/up
-projection, SiLU-gated product, down projection per expert, under torchtitan's
-token dispatcher with MXFP8 grouped GEMMs patched in, ``port_mxfp8.py:175-194``)
-built from this library's pieces:
+projection, SiLU-gated product, down projection per expert, and its backward
+``dh = dC @ w2``, SiLU backward, ``dx = d_gate @ w1 + d_up @ w3`` and both
+weight gradients, under torchtitan's token dispatcher with MXFP8 grouped GEMMs
+patched in, ``port_mxfp8.py:175-194``) built from this library's pieces:
 
 forward   dispatch x -> quantize (1x32 and 32x1 in one pass) -> gate/up
           grouped fwd -> swiglu fused with its quantisation -> down grouped
           fwd -> combine (weighted by router probs)
 backward  dispatch dy along the same plan -> quantize (both directions) ->
           down dgrad (grouped fwd against the pre-quantised transposed down
-          weights) -> down wgrad -> swiglu backward fused with its 32x1
-          quantisation -> gate/up wgrad
+          weights) -> down wgrad -> swiglu backward fused with its 1x32 and
+          32x1 quantisation -> gate/up dgrad (grouped fwd against the
+          pre-quantised transposed gate/up weights, one K=2I contraction for
+          d_gate @ w1 + d_up @ w3) -> its rows back home, summed over each
+          token's choices -> gate/up wgrad
 
 Weights are quantised once (static between optimiser steps).  With a comm
-stream the dy dispatch runs under the forward GEMMs and the combine under the
-backward GEMMs; only the x dispatch (and its count exchange) sits in front of
-the first GEMM.  The activation gradient of the gate/up projection (dx) is not
-computed: the benchmark layer step covers the forward and both weight
-gradients.
+stream the dy dispatch runs under the forward GEMMs and the two returns under
+the backward GEMMs; only the x dispatch (and its count exchange) sits in front
+of the first GEMM.
 """
 from __future__ import annotations
 
 from contextlib import nullcontext
+from typing import NamedTuple
 
 import torch
 
 from . import _lib, ops
 from .ep import ExpertParallel
+
+
+class LayerStep(NamedTuple):
+    """Results of one ``ExpertFFN.step``: the combined output [n, H], the
+    gradient of the token inputs [n, H] (None when not computed), the weight
+    gradients [E_local, 2I, H] and [E_local, H, I], and the dispatch plan."""
+    out: torch.Tensor
+    dx: torch.Tensor | None
+    dw_gate_up: torch.Tensor
+    dw_down: torch.Tensor
+    plan: object
 
 
 class ExpertFFN:
@@ -36,15 +50,18 @@ class ExpertFFN:
 
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
-                 wgrad_dtype: torch.dtype = torch.bfloat16):
-        """With a comm stream, the dy dispatch and the combine's return run
-        beside the GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM
-        blocks while they do, and runs the peer copies only there.
-        wgrad_dtype is the weight gradients' dtype: bf16 by default, as the
-        reference's wgrad returns them (``wgrad_fused.py:41``), or fp32."""
+                 wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True):
+        """With a comm stream, the dy dispatch and the returns run beside the
+        GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
+        they do, and runs the peer copies only there.  wgrad_dtype is the
+        weight gradients' dtype: bf16 by default, as the reference's wgrad
+        returns them (``wgrad_fused.py:41``), or fp32.  compute_dx: also
+        compute the gradient of the token inputs (the gate/up dgrad and its
+        return to the tokens' ranks)."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
+        self.compute_dx = compute_dx
         self.ep = ep
         E, I2, H = w_gate_up.shape
         E2, H2, I = w_down.shape
@@ -59,6 +76,12 @@ class ExpertFFN:
         q, s = ops.quantize_rowwise(wdt.view(E * I, H))
         self.wdt = (q.view(E, I, H), s.view(E, I, H // 32))
         del wdt
+        self.wgut = None
+        if compute_dx:                                       # [E, H, 2I] for dx = dgu . W_gu
+            wgut = w_gate_up.transpose(1, 2).contiguous()
+            q, s = ops.quantize_rowwise(wgut.view(E * H, 2 * I))
+            self.wgut = (q.view(E, H, 2 * I), s.view(E, H, 2 * I // 32))
+            del wgut
         self.comm = comm_stream
         self.reserve = reserve_sms if comm_stream is not None else 0
         if self.reserve:
@@ -68,6 +91,7 @@ class ExpertFFN:
         else:
             self.gemm_sms = 0
         self.marks = None           # optional list of (name, cuda event) for profiling
+        self.trace = None           # optional dict: a step keeps its intermediates here
 
     def _mark(self, name):
         if self.marks is not None:
@@ -84,12 +108,15 @@ class ExpertFFN:
         return ops.grouped_wgrad(go[0], ia[0], offs, go[1], ia[1], out_dtype=self.wgrad_dtype,
                                  offs_kind=_lib.OFFS_SIZES, num_groups=self.E)
 
-    def step(self, x, expert_ids, probs, dy):
-        """Forward and weight gradients of one layer step.  x, dy [n, H] bf16,
-        expert_ids [n, k] int32, probs [n, k] fp32.  Returns (out [n, H] bf16,
-        dW_gate_up [E_local, 2I, H], dW_down [E_local, H, I] (wgrad_dtype), plan).
-        dy is the gradient of each routed row's expert output: it is sent to
-        every expert the token chose, unweighted."""
+    def _keep(self, **kw):
+        if self.trace is not None:
+            self.trace.update(kw)
+
+    def step(self, x, expert_ids, probs, dy) -> LayerStep:
+        """Forward and backward of one layer step.  x, dy [n, H] bf16,
+        expert_ids [n, k] int32, probs [n, k] fp32.  dy is the gradient of
+        each routed row's expert output: it is sent to every expert the token
+        chose, unweighted, and dx sums the k rows' input gradients."""
         ep = self.ep
         main = torch.cuda.current_stream()
         comm = self.comm
@@ -97,13 +124,15 @@ class ExpertFFN:
         self._mark("start")
         x_local, plan = ep.dispatch(x, expert_ids)
         offs = plan.group_rows
-        self._mark("dispatch")
+        self._mark("dispatch_x")
         if comm is not None:
             comm.wait_stream(main)
         with side():
             dy_local = ep.dispatch_like(dy, plan)
             dy_ready = torch.cuda.Event()
             dy_ready.record()
+        if comm is None:
+            self._mark("dispatch_dy")
         xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
         self._mark("quantize_x")
         with ops.gemm_sm_limit(self.gemm_sms):             # beside the dy exchange
@@ -117,17 +146,31 @@ class ExpertFFN:
             comm.wait_stream(main)
         with side():
             ret = ep.combine_send(y_local, plan)
+        if comm is None:
+            self._mark("return_y")
         main.wait_event(dy_ready)
         dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
         self._mark("quantize_dy")
-        with ops.gemm_sm_limit(self.gemm_sms):             # beside the combine's return
+        with ops.gemm_sm_limit(self.gemm_sms):             # beside the y return
             dh = self._fwd((dyq, dys), self.wdt, offs)
             self._mark("dgrad_down")
             dw_d = self._wgrad((go_d, gos_d), (ia_d, ias_d), offs)
         self._mark("wgrad_down")
-        _, _, go_g, gos_g = ops.swiglu_bwd_quantize(gu, dh)  # dgu is never written in bf16
-        self._mark("quantize_gate_up")
-        dw_gu = self._wgrad((go_g, gos_g), (ia_g, ias_g), offs)
+        dgq, dgs, go_g, gos_g = ops.swiglu_bwd_quantize(gu, dh, rowwise=self.compute_dx)
+        self._mark("swiglu_bwd_quantize")                  # dgu is never written in bf16
+        ret_dx = dx_local = None
+        if self.compute_dx:
+            with ops.gemm_sm_limit(self.gemm_sms):
+                dx_local = self._fwd((dgq, dgs), self.wgut, offs)
+            self._mark("dgrad_gate_up")
+            if comm is not None:
+                comm.wait_stream(main)
+            with side():
+                ret_dx = ep.combine_send(dx_local, plan, buffer="ret_dx")
+            if comm is None:
+                self._mark("return_dx")
+        with ops.gemm_sm_limit(self.gemm_sms):             # beside the dx return
+            dw_gu = self._wgrad((go_g, gos_g), (ia_g, ias_g), offs)
         self._mark("wgrad_gate_up")
         if comm is not None:
             # Every later use of memory from either stream is ordered after
@@ -135,12 +178,22 @@ class ExpertFFN:
             # stream waits on main), so no record_stream is needed.
             main.wait_stream(comm)
         out = ep.combine_finish(ret, plan, probs)
+        dx = ep.combine_finish(ret_dx, plan, None) if ret_dx is not None else None
         self._mark("combine")
-        return out, dw_gu, dw_d, plan
+        if self.trace is not None:
+            self._keep(x_local=x_local.clone(), dy_local=dy_local.clone(), xq=xq, xs=xs, ia_g=ia_g,
+                       ias_g=ias_g, gu=gu, hq=hq, hs=hs, ia_d=ia_d, ias_d=ias_d, y_local=y_local,
+                       dyq=dyq, dys=dys, go_d=go_d, gos_d=gos_d, dh=dh, dgq=dgq, dgs=dgs, go_g=go_g,
+                       gos_g=gos_g, dx_local=dx_local, ret=ret.clone(),
+                       ret_dx=None if ret_dx is None else ret_dx.clone())
+        return LayerStep(out, dx, dw_gu, dw_d, plan)
 
     def gemm_flops(self, plan) -> dict:
-        """Algorithmic FLOPs of the step's five grouped GEMMs on real rows."""
+        """Algorithmic FLOPs of the step's grouped GEMMs on real rows."""
         r, H, I = plan.recv_rows, self.H, self.I
-        return {"fwd_gate_up": 2 * r * 2 * I * H, "fwd_down": 2 * r * H * I,
-                "dgrad_down": 2 * r * I * H, "wgrad_down": 2 * r * H * I,
-                "wgrad_gate_up": 2 * r * 2 * I * H}
+        f = {"fwd_gate_up": 2 * r * 2 * I * H, "fwd_down": 2 * r * H * I,
+             "dgrad_down": 2 * r * I * H, "wgrad_down": 2 * r * H * I,
+             "wgrad_gate_up": 2 * r * 2 * I * H}
+        if self.compute_dx:
+            f["dgrad_gate_up"] = 2 * r * H * 2 * I
+        return f

@@ -136,6 +136,58 @@ def test_expert_parallel_gloo(world, balanced):
         assert res[r] == "ok", res[r]
 
 
+class _DroppingOps(OracleEpOps):
+    """Routes like the CUDA kernel does with an out-of-range expert id: the
+    slot is counted nowhere (its send position is never written)."""
+
+    def route(self, expert_ids, num_experts, slot_of_expert=None):
+        ids = expert_ids.cpu().numpy()
+        ok = (ids >= 0) & (ids < num_experts)
+        c, sr, sp = ep_oracle.route(np.where(ok, ids, 0), num_experts)
+        c = np.bincount(ids[ok].reshape(-1), minlength=num_experts).astype(np.int32)
+        return torch.from_numpy(c), torch.from_numpy(sr), torch.from_numpy(sp)
+
+
+def _bad_ids_worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from conftest import load_pkg
+        ep = load_pkg().ep
+        E, k, H = 8, 2, 64
+        par = ep.ExpertParallel(E, ops=_DroppingOps(), transport="p2p")
+        ids, x, _ = make_rank_inputs(rank, 16, k, E, H)
+        if rank == 1:
+            ids[3, 0], ids[9, 1] = E, -1          # two routing slots with no expert
+        try:
+            par.dispatch(torch.from_numpy(x).to(torch.bfloat16), torch.from_numpy(ids))
+            msg = "no error"
+        except ValueError as e:
+            msg = "raised" if "(rank 1: 2)" in str(e) else str(e)
+        dist.barrier()                            # both ranks got here: nobody hangs
+        dist.destroy_process_group()
+        q.put((rank, msg))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+def test_p2p_dispatch_refuses_unrouted_slots_on_every_rank():
+    """An expert id outside [0, E) on one rank makes every rank raise from the
+    gathered counts, before any peer store (no rank is left waiting)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_bad_ids_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "raised", 1: "raised"}, res
+
+
 @pytest.mark.parametrize("world", [1, 3, 4])
 def test_p2p_plan_places_rows_like_regroup(world):
     """Every send position lands where the regroup layout puts it, and every

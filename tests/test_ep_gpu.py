@@ -2,9 +2,9 @@
 maps and row moves; the weighted combine within one bf16 ulp of the oracle's
 fp32 sum; swiglu within 1e-2 relative of a torch fp32 reference), one expert
 layer through dispatch -> MXFP8 GEMMs -> combine against fp64, the whole
-moe.ExpertFFN step (forward and both weight gradients) against a host
-restatement, and a world-size-2 NCCL dispatch/combine when the box has two
-GPUs."""
+moe.ExpertFFN step (forward, input gradient and both weight gradients)
+against a host restatement, and a world-size-2 NCCL dispatch/combine when
+the box has two GPUs."""
 import multiprocessing as mp
 import os
 
@@ -210,6 +210,47 @@ def test_p2p_dispatch_rejects_rows_past_capacity(mxg, cuda_dev):
     assert torch.all(guard == 0)
 
 
+def test_p2p_dispatch_skips_unrouted_positions_and_bad_source_rows(mxg, cuda_dev):
+    """Routing slots with expert ids -1 and E are counted nowhere, so their
+    send positions (past slot_start[E]) stay unwritten: the dispatch must not
+    read them even when they hold garbage, and a source row outside the
+    source tensor is skipped and reported.  The other rows land as the oracle
+    places them."""
+    E, k, H, n = 4, 2, 64, 100
+    ids, x, _ = make_rank_inputs(0, n, k, E, H)
+    ids[5, 0], ids[17, 1], ids[60, 0] = -1, E, E
+    ep, p2p = mxg.ep.CudaEpOps(), mxg.ep.CudaP2POps()
+    c, sr, sp = ep.route(torch.from_numpy(ids).to(cuda_dev), E)
+    assert mxg.device_error() == mxg._lib.MXG_ERR_INVALID_ARGUMENT   # route reports the ids
+    routed = int(c.sum())
+    assert routed == n * k - 3
+    sr[routed:] = 1 << 30                       # garbage past the routed positions
+    ok = (ids >= 0) & (ids < E)
+    want, _, _ = ep_oracle.simulate([x], [np.where(ok, ids, 0)], E)
+    C = c.view(1, E)
+    m_pad = int(((c.cpu().numpy() + 31) // 32 * 32).sum())
+    pl = p2p.plan(C, 0, 32, m_pad, routed)
+    buf = torch.zeros(m_pad + 8, H, dtype=torch.bfloat16, device=cuda_dev)
+    ptrs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda_dev)
+    xb = _bf16(x, cuda_dev)
+    p2p.dispatch(xb, sr, pl[0], pl[1], E, 0, ptrs, buf.shape[0])
+    assert mxg.device_error() == 0
+    # the oracle routed the bad slots to expert 0: compare the other experts' rows
+    got = buf[:m_pad].float().cpu().numpy()
+    gr = pl[2].cpu().numpy()
+    g0 = int(gr[0])
+    ref_rows = want[0][0]
+    ref_g0 = int(((np.sum(np.where(ok, ids, 0) == 0) + 31) // 32) * 32)
+    assert np.array_equal(got[g0:], ref_rows[ref_g0:])
+    # a source row index outside x: skipped, reported, nothing else disturbed
+    sr2 = sr.clone()
+    sr2[0] = n + 3
+    buf.zero_()
+    p2p.dispatch(xb, sr2, pl[0], pl[1], E, 0, ptrs, buf.shape[0])
+    assert mxg.device_error() == mxg._lib.MXG_ERR_INVALID_ARGUMENT
+    assert torch.all(buf[m_pad:] == 0)
+
+
 def _nccl_worker(rank, world, port, q, transport="nccl"):
     try:
         import datetime
@@ -306,6 +347,7 @@ def _ffn_emulation(x, dy, wgu, wd, ids, p, E):
     res = {}
     for quant in (True, False):
         out = np.zeros((n, H))
+        dx = np.zeros((n, H))
         dwgu = np.zeros((E, 2 * I, H))
         dwd = np.zeros((E, H, I))
         for e in range(E):
@@ -329,19 +371,22 @@ def _ffn_emulation(x, dy, wgu, wd, ids, p, E):
             if quant:
                 dwd[e] = q_col(dye) @ q_col(h).T
                 dwgu[e] = q_col(dgu) @ q_col(xe).T
+                dxe = bf(q_row(dgu) @ q_row(np.ascontiguousarray(wgu[e].T)).T)
             else:
                 dwd[e] = dye.T @ h
                 dwgu[e] = dgu.T @ xe
+                dxe = dgu @ wgu[e]
             for r, (t, j) in enumerate(rows):
                 out[t] += p[t, j] * y[r]
-        res[quant] = (out, dwgu, dwd)
+                dx[t] += dxe[r]
+        res[quant] = (out, dx, dwgu, dwd)
     return res
 
 
 @pytest.mark.parametrize("wgrad_dtype", [torch.bfloat16, torch.float32])
 def test_expert_ffn_world1(mxg, cuda_dev, wgrad_dtype):
-    """moe.ExpertFFN on one rank: the combined output and both weight
-    gradients against a host restatement of the same MXFP8 layer step
+    """moe.ExpertFFN on one rank: the combined output, the input gradient and
+    both weight gradients against a host restatement of the same MXFP8 layer step
     (relative Frobenius <= 3e-2: the fused SwiGLU quantisers round their fp32
     inputs once, the restatement through bf16) and against the unquantised
     fp64 layer (<= 0.12; MXFP8 alone costs ~0.066 here)."""
@@ -355,14 +400,14 @@ def test_expert_ffn_world1(mxg, cuda_dev, wgrad_dtype):
     p = (p / p.sum(1, keepdims=True)).astype(np.float32)
     layer = mxg.moe.ExpertFFN(mxg.ExpertParallel(E), wgu.to(cuda_dev), wd.to(cuda_dev),
                               wgrad_dtype=wgrad_dtype)
-    out, dw_gu, dw_d, plan = layer.step(x.to(cuda_dev), torch.from_numpy(ids).to(cuda_dev),
-                                        torch.from_numpy(p).to(cuda_dev), dy.to(cuda_dev))
+    res = layer.step(x.to(cuda_dev), torch.from_numpy(ids).to(cuda_dev),
+                     torch.from_numpy(p).to(cuda_dev), dy.to(cuda_dev))
     assert mxg.device_error() == 0
-    assert dw_gu.dtype == wgrad_dtype and dw_d.dtype == wgrad_dtype
+    assert res.dw_gate_up.dtype == wgrad_dtype and res.dw_down.dtype == wgrad_dtype
     ref = _ffn_emulation(x.float().numpy().astype(np.float64), dy.float().numpy().astype(np.float64),
                          wgu.float().numpy().astype(np.float64), wd.float().numpy().astype(np.float64),
                          ids, p.astype(np.float64), E)
-    got = [t.float().cpu().numpy().astype(np.float64) for t in (out, dw_gu, dw_d)]
-    for name, g, rq, rf in zip(("out", "dw_gate_up", "dw_down"), got, ref[True], ref[False]):
+    got = [t.float().cpu().numpy().astype(np.float64) for t in (res.out, res.dx, res.dw_gate_up, res.dw_down)]
+    for name, g, rq, rf in zip(("out", "dx", "dw_gate_up", "dw_down"), got, ref[True], ref[False]):
         eq, ef = orc_mod.rel_frobenius(g, rq), orc_mod.rel_frobenius(g, rf)
         assert eq <= 3e-2 and ef <= 0.12, (name, eq, ef)

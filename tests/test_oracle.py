@@ -24,6 +24,43 @@ def test_rceil_scale_exhaustive_over_bf16(orc):
     assert orc.rceil_scale_from_amax_bits(np.array([0, 0x7F80, 0x7FC0]))[...].tolist() == [0, 254, 255]
 
 
+def test_rceil_scale_pinned_to_third_party_ceil_ue8m0(orc):
+    """The RCEIL byte against code this repository did not write: DeepGEMM's
+    power-of-two scale rule ``2**ceil(log2(amax / 448))`` as flashinfer ships
+    it (``flashinfer.testing.utils._ceil_to_ue8m0``, flashinfer 0.6.11), for
+    every positive finite bf16 amax, clamped to the E8M0 range as the
+    ``mxfp8_rceil`` recipe does (byte = clamp(exponent, -127, 127) + 127)."""
+    fi = pytest.importorskip("flashinfer.testing.utils")
+    import torch
+    bits = np.arange(0x0001, 0x7F80, dtype=np.uint32)
+    got = orc.rceil_scale_from_amax_bits(bits).astype(np.int64)
+    amax = torch.from_numpy(bits.astype(np.int32)).to(torch.int16).view(torch.bfloat16)
+    sf = fi._ceil_to_ue8m0(amax.float() / 448.0)
+    want = torch.log2(sf).round().to(torch.int64).clamp(-127, 127) + 127
+    assert np.array_equal(got, want.numpy())
+
+
+def test_e4m3_elements_pinned_to_torch_cast(orc):
+    """Element codes against torch's own float32 -> float8_e4m3fn cast (round
+    to nearest even), applied to x * 2**(127 - byte) as the recipe scales
+    them, on seeded bf16 blocks spanning many binades (blocks whose scale byte
+    is 0 are left to the torchao-restatement fixture: the recipe does not
+    scale those)."""
+    import torch
+    g = np.random.default_rng(7)
+    x = g.standard_normal((512, 256)) * np.exp2(g.integers(-60, 60, (512, 1)))
+    x[::7, 3] = 0.0
+    x[5] = 448.0 * np.exp2(-20)                     # exact powers at the scale boundary
+    xb = orc.f32_to_bf16_bits(x.astype(np.float32))
+    q, s = orc.quantize_rowwise(xb)
+    assert (s > 0).all()
+    xf = torch.from_numpy(orc.bf16_bits_to_f32(xb))
+    factor = torch.from_numpy(np.exp2(127.0 - s.astype(np.float64)).astype(np.float32))
+    scaled = xf.view(512, 8, 32) * factor.view(512, 8, 1)
+    want = scaled.to(torch.float8_e4m3fn).view(torch.uint8).reshape(512, 256).numpy()
+    assert np.array_equal(q, want)
+
+
 def test_e4m3_roundtrip_all_codes(orc):
     codes = np.arange(256, dtype=np.uint8)
     vals = orc.E4M3_DECODE[codes]
