@@ -659,7 +659,7 @@ class EpLayerBench:
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
                  transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16", experts=EP_EXPERTS,
-                 logp=None, compute_dx=True):
+                 logp=None, compute_dx=True, copy_engines=False):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -686,7 +686,8 @@ class EpLayerBench:
         self.wgrad_dtype = wgrad_dtype
         self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm,
                                      wgrad_dtype=torch.float32 if wgrad_dtype == "fp32" else torch.bfloat16,
-                                     reserve_sms=reserve_sms, compute_dx=compute_dx)
+                                     reserve_sms=reserve_sms, compute_dx=compute_dx,
+                                     copy_engines=copy_engines)
         del w_gu, w_d
         torch.cuda.synchronize()
 
@@ -961,7 +962,8 @@ def run_ep_mxg(args, rank, world, local):
     pkg()._lib.load()
     lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
                       transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
-                      wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx)
+                      wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx,
+                      copy_engines=args.copy_engines)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -994,7 +996,7 @@ def run_ep_mxg(args, rank, world, local):
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
            "data": "synthetic",
            "config": ep_config(world, args.placement, args.overlap, r["transport"], r["reserve_sms"],
-                               args.ep_wgrad_dtype, args.seed, not args.no_dx),
+                               args.ep_wgrad_dtype, args.seed, not args.no_dx, args.copy_engines),
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
                "padded_rows_this_rank", "segments_ms_rank0", "exchange_ms_rank0", "gemm_ms_rank0",
@@ -1032,7 +1034,7 @@ def ep_flops(rows, dx=True):
     return (18 if dx else 14) * int(rows) * HIDDEN * INTER
 
 
-def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx):
+def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx, copy_engines=False):
     """The config object of a config-4 line (the reference arm prints the same)."""
     rows, padded = ep_routing_stats(world, seed, placement)
     flops_rank = ep_flops(rows[0], dx)
@@ -1044,6 +1046,7 @@ def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, se
             "tokens_per_gpu": EP_TOKENS, "topk": EP_TOPK, "zipf_s": EP_ZIPF,
             "hidden": HIDDEN, "intermediate": INTER, "placement": placement,
             "comm_overlap": overlap, "transport": transport, "reserved_sms": reserve_sms,
+            "exchange_engine": "copy engines" if (overlap and copy_engines) else "SM kernels",
             "dw_dtype": wgrad_dtype + (" (the reference's wgrad output dtype)" if wgrad_dtype == "bf16" else ""),
             "routed_rows_per_gpu": EP_TOKENS * EP_TOPK, "max_rows_received_per_gpu": rows_max,
             "padded_rows": padded,  # rank 0's
@@ -1256,7 +1259,7 @@ def run_reference_layer(args, world):
            "config": ep_config(world, args.placement, args.overlap,
                                "nccl" if args.transport == "nccl" else "p2p",
                                args.reserve_sms if args.overlap else 0, args.ep_wgrad_dtype, args.seed,
-                               not args.no_dx),
+                               not args.no_dx, args.copy_engines),
            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
                             "kind": "port", "sample": sample},
            "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1338,6 +1341,8 @@ def main():
     ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
                     help="weight-gradient dtype of the config-4 expert layer (bf16: the reference's "
                          "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
+    ap.add_argument("--copy-engines", action="store_true",
+                    help="EP layer with --overlap: the dy dispatch and the returns as copy-engine runs")
     ap.add_argument("--no-dx", action="store_true",
                     help="EP layer: skip the gate/up dgrad (input gradient) and its return")
     ap.add_argument("--no-nccl-layer", action="store_true",

@@ -285,6 +285,20 @@ MXG_API int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t*
                               const uint64_t* peer_bufs, int world, int64_t capacity_rows,
                               int max_blocks, void* stream);
 
+/* Contiguous runs of rows moved by the GPU's copy engines instead of SMs, so
+ * an exchange can run beside tensor-core kernels without taking their SMs:
+ * run i copies rows [src_row[i], src_row[i] + rows[i]) of src to rows
+ * [dst_row[i], dst_row[i] + rows[i]) of dst_bufs[dst_buf[i]], one
+ * cudaMemcpyAsync per run on the given stream.  The run tables and dst_bufs
+ * are HOST arrays; dst_bufs may hold peer addresses (mxg_peer_open).  Every
+ * run is checked against src_rows and dst_rows before any copy is issued
+ * (MXG_ERR_INVALID_ARGUMENT).  The copies only write; the caller orders the
+ * ranks around them as around mxg_ep_dispatch_p2p. */
+MXG_API int mxg_copy_runs(const void* src, int64_t src_rows, int64_t row_bytes, const int64_t* src_row,
+                          const int64_t* dst_row, const int64_t* rows, const int32_t* dst_buf,
+                          int64_t n_runs, const uint64_t* dst_bufs, int n_dst, int64_t dst_rows,
+                          void* stream);
+
 /* Zero the rows q < m_pad of buf with back_rank[q] < 0. */
 MXG_API int mxg_ep_zero_pad_rows(void* buf, int64_t row_bytes, const int32_t* back_rank,
                                  int64_t m_pad, void* stream);

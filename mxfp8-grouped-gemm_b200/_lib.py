@@ -77,6 +77,8 @@ _PROTOS = {
     "mxg_ep_return_p2p": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_int, _c_i64, _c_int,
                                    _vp]),
     "mxg_ep_zero_pad_rows": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp]),
+    "mxg_copy_runs": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _vp, _c_int, _c_i64,
+                               _vp]),
     "mxg_set_gemm_sm_limit": (_c_int, [_c_int]),
     "mxg_get_gemm_sm_limit": (_c_int, []),
     "mxg_quantize_dual": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),

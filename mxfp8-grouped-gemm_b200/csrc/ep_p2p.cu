@@ -391,3 +391,31 @@ extern "C" int mxg_ep_zero_pad_rows(void* buf, int64_t row_bytes, const int32_t*
       reinterpret_cast<uint4*>(buf), row_bytes / 16, back_rank, m_pad);
   return cuda_status(cudaGetLastError());
 }
+
+extern "C" int mxg_copy_runs(const void* src, int64_t src_rows, int64_t row_bytes,
+                             const int64_t* src_row, const int64_t* dst_row, const int64_t* rows,
+                             const int32_t* dst_buf, int64_t n_runs, const uint64_t* dst_bufs,
+                             int n_dst, int64_t dst_rows, void* stream) {
+  if (n_runs < 0 || src_rows < 0 || row_bytes < 0 || n_dst < 0 || dst_rows < 0)
+    return MXG_ERR_INVALID_ARGUMENT;
+  if (n_runs == 0 || row_bytes == 0) return MXG_OK;
+  if (!src || !src_row || !dst_row || !rows || !dst_buf || !dst_bufs) return MXG_ERR_INVALID_ARGUMENT;
+  for (int64_t i = 0; i < n_runs; ++i) {  // every run in bounds before the first copy
+    const int64_t n = rows[i];
+    if (n < 0 || src_row[i] < 0 || src_row[i] > src_rows - n || dst_row[i] < 0 ||
+        dst_row[i] > dst_rows - n || dst_buf[i] < 0 || dst_buf[i] >= n_dst || dst_bufs[dst_buf[i]] == 0)
+      return MXG_ERR_INVALID_ARGUMENT;
+  }
+  int st = check_device();
+  if (st) return st;
+  const uint8_t* s8 = reinterpret_cast<const uint8_t*>(src);
+  for (int64_t i = 0; i < n_runs; ++i) {
+    if (rows[i] == 0) continue;
+    uint8_t* d8 = reinterpret_cast<uint8_t*>(dst_bufs[dst_buf[i]]);
+    const cudaError_t e = cudaMemcpyAsync(d8 + dst_row[i] * row_bytes, s8 + src_row[i] * row_bytes,
+                                          size_t(rows[i] * row_bytes), cudaMemcpyDefault,
+                                          (cudaStream_t)stream);
+    if (e != cudaSuccess) return MXG_ERR_CUDA;
+  }
+  return MXG_OK;
+}

@@ -42,16 +42,11 @@
 namespace mxg {
 
 constexpr int kBM = 128;                 // A rows per CTA (a pair covers 256)
-constexpr int kBNMax = 240;              // max B rows per pair tile (MMA N)
-constexpr int kBHalf = kBNMax / 2;       // B rows each CTA of the pair loads
+constexpr int kBNMax = 240;              // max B rows per pair tile (MMA N) of any mode
 constexpr int kBK = 128;                 // contraction bytes per stage
-constexpr int kStages = 6;
 constexpr int kABytes = kBM * kBK;       // 16 KiB
-constexpr int kBBytes = kBHalf * kBK;    // 15 KiB
 constexpr int kSfaBytes = 512;           // 128 rows x 4 scales, UTCCP layout
 constexpr int kSfbBytes = 1024;          // 2 x (128 rows x 4 scales)
-constexpr uint32_t kStageTxPerCta = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = 256;     // accumulator buffer i at column 256*i
 // Scale factors live in two TMEM buffers used by alternate stages, so the
@@ -61,6 +56,38 @@ constexpr uint32_t kSfCol0 = 240, kSfCol1 = 496;
 constexpr uint32_t kSfbOff = 4;
 
 enum { MODE_FWD = 0, MODE_WGRAD = 1 };
+
+// Per-mode shape of the kernel.  The wgrad's epilogue writes 128 x N fp32
+// (or bf16) per CTA and tile, about as long as a small expert's whole main
+// loop, so it runs eight epilogue warps -- two per TMEM lane quarter, each
+// with half of the tile's columns.  Their staging buffers fit beside six
+// pipeline stages (fewer stages starve the MMA: the operand loads need about
+// five k-steps of lead) with B tiles of up to 224 rows.  The forward's bf16
+// epilogue is short next to its 56-step main loop and keeps four epilogue
+// warps and 240-row B tiles.
+//   warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer, 6-9 epilogue (wgrad)
+#ifndef MXG_WGRAD_EPI_WARPS
+#define MXG_WGRAD_EPI_WARPS 4
+#endif
+#ifndef MXG_WGRAD_BN
+#define MXG_WGRAD_BN 240
+#endif
+#define MXG_WGRAD_EPI_WARPS_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_EPI_WARPS : 4)
+#define MXG_WGRAD_BN_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_BN : 240)
+template <int MODE>
+struct Cfg {
+  static constexpr int kStages = 6;
+  static constexpr int kEpiWarps = MXG_WGRAD_EPI_WARPS_FOR(MODE);
+  static constexpr int kThreads = 32 * (kEpiWarps + 2);
+  static constexpr int kBN = MXG_WGRAD_BN_FOR(MODE);            // max B rows per pair tile
+  static constexpr int kBHalf = kBN / 2;                       // B rows each CTA loads
+  static constexpr int kBBytes = kBHalf * kBK;
+  static constexpr uint32_t kStageTxPerCta = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+};
+__host__ __device__ constexpr int bn_max(int mode) {
+  return mode == MODE_WGRAD ? Cfg<MODE_WGRAD>::kBN : Cfg<MODE_FWD>::kBN;
+}
+static_assert(Cfg<MODE_FWD>::kBN <= kBNMax && Cfg<MODE_WGRAD>::kBN <= kBNMax, "TMEM columns");
 
 // ---- scheduler output (int32 words in the workspace) ------------------------
 //   [0] tiles  [1] A scale chunks  [2] B scale chunks  [3] first row after the
@@ -81,7 +108,7 @@ struct MetaView {
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 // Balanced split of `ext` rows into `nt` tiles of whole 16-row units (each
-// at most kBNMax rows).  Returns the first row and the row count of tile `i`.
+// at most the mode's B tile rows).  Returns the first row and the row count of tile `i`.
 __host__ __device__ inline void split_rows(int ext, int nt, int i, int& n0, int& nlen) {
   const int units = (ext + 15) / 16;
   const int q = units / nt, r = units % nt;
@@ -193,10 +220,10 @@ __global__ void __launch_bounds__(MXG_MAX_GROUPS) schedule_kernel(SchedArgs a) {
   const int mbp = ceil_div(a.n_out, 2 * kBM);  // pairs of 128-row A blocks
   if (tid < E && !any_bad) {
     if (a.mode == MODE_FWD) {
-      nt = ceil_div(len, kBNMax);
+      nt = ceil_div(len, bn_max(MODE_FWD));
       kb = ceil_div(a.k_fwd, kBK);
     } else {
-      nt = ceil_div(a.n_ext, kBNMax);
+      nt = ceil_div(a.n_ext, bn_max(MODE_WGRAD));
       kb = ceil_div(len, kBK);
     }
     tiles = mbp * nt;
@@ -451,14 +478,16 @@ struct GemmArgs {
   int wgrad_tma_store;  // wgrad output row stride is 16-byte aligned: store via TMA
 };
 
-struct __align__(1024) SmemLayout {
-  uint8_t a[kStages][kABytes];
-  uint8_t b[kStages][kBBytes];
-  uint8_t sfa[kStages][kSfaBytes];
-  uint8_t sfb[kStages][kSfbBytes];
-  alignas(1024) uint8_t epi[4][4096];  // per epilogue warp: 4 KiB staging (two 2 KiB slots), swizzled
-  uint64_t full[kStages];      // leader: both CTAs' loads of the stage landed
-  uint64_t empty[kStages];     // each CTA: the pair MMA finished reading the stage
+template <int S, int EW, int BB>
+struct __align__(1024) SmemT {
+  static constexpr int kStages = S;
+  uint8_t a[S][kABytes];
+  uint8_t b[S][BB];
+  uint8_t sfa[S][kSfaBytes];
+  uint8_t sfb[S][kSfbBytes];
+  alignas(1024) uint8_t epi[EW][4096];  // per epilogue warp: 4 KiB staging (two 2 KiB slots), swizzled
+  uint64_t full[S];            // leader: both CTAs' loads of the stage landed
+  uint64_t empty[S];           // each CTA: the pair MMA finished reading the stage
   uint64_t acc_full[2];        // each CTA: accumulator buffer complete
   uint64_t acc_empty[2];       // leader: both CTAs' epilogues drained the buffer
   uint64_t drain;
@@ -466,82 +495,116 @@ struct __align__(1024) SmemLayout {
   uint32_t tmem_base;
   int abort_flag;
   int num_tiles;
+  // first tile of each group (the per-tile binary search); the other
+  // per-group fields are read from the scheduler's table in global memory
   int tile_start[MXG_MAX_GROUPS + 1];
-  int g_start[MXG_MAX_GROUPS];
-  int g_len[MXG_MAX_GROUPS];
-  int g_nt[MXG_MAX_GROUPS];
-  int g_kb[MXG_MAX_GROUPS];
-  int g_asf[MXG_MAX_GROUPS + 1];
-  int g_bsf[MXG_MAX_GROUPS + 1];
 };
-constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;
+template <int MODE>
+using SmemOf = SmemT<Cfg<MODE>::kStages, Cfg<MODE>::kEpiWarps, Cfg<MODE>::kBBytes>;
+template <int MODE>
+constexpr size_t smem_bytes() { return sizeof(SmemOf<MODE>) + 1024; }
 // swizzled tiles must start on 1024-byte boundaries (the swizzle pattern is
 // taken from address bits 4-9)
-static_assert(offsetof(SmemLayout, a) % 1024 == 0 && kABytes % 1024 == 0, "A tile alignment");
-static_assert(offsetof(SmemLayout, b) % 1024 == 0 && kBBytes % 1024 == 0, "B tile alignment");
-static_assert(offsetof(SmemLayout, epi) % 1024 == 0, "epilogue staging alignment");
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+template <class L>
+constexpr bool layout_ok() {
+  return offsetof(L, a) % 1024 == 0 && offsetof(L, b) % 1024 == 0 && offsetof(L, epi) % 1024 == 0 &&
+         kABytes % 1024 == 0 && sizeof(L::b[0]) % 1024 == 0;
+}
+static_assert(layout_ok<SmemOf<MODE_FWD>>() && layout_ok<SmemOf<MODE_WGRAD>>(), "tile alignment");
+static_assert(smem_bytes<MODE_FWD>() <= 232448 && smem_bytes<MODE_WGRAD>() <= 232448,
+              "shared memory budget");
 
 struct TileInfo {
   int e, mb, nt, n0, nlen, kb_count, klen, k0, a_row, b_row, sfa0, sfb0;
 };
 
-// Pair tile t as seen by CTA `rank` of the pair: its own 128-row A block
-// (mb = 2 * pair block + rank) and the pair's B rows [b_row, b_row + nlen).
+// Walks one CTA's pair tiles in increasing order (t = pair, pair + npairs,
+// ...) and decodes tile t as seen by CTA `rank` of the pair: its own 128-row
+// A block (mb = 2 * pair block + rank) and the pair's B rows [b_row, b_row +
+// nlen).  The current group's fields stay cached, so the next tile costs one
+// division; a binary search over the groups' first tiles happens only for
+// the first tile (a per-tile search and the table loads cost ~700 cycles).
 template <int MODE>
-__device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const GemmArgs& g, int t,
-                                                int rank) {
-  TileInfo ti;
-  int lo = 0, hi = g.E - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s.tile_start[mid] <= t) lo = mid; else hi = mid - 1;
-  }
-  ti.e = lo;
-  const int local = t - s.tile_start[lo];
-  const int nt_count = s.g_nt[lo];
-  const int mbp = local / nt_count;
-  ti.nt = local - mbp * nt_count;
-  ti.mb = 2 * mbp + rank;
-  const int ext = MODE == MODE_FWD ? s.g_len[lo] : g.n_ext;
-  split_rows(ext, nt_count, ti.nt, ti.n0, ti.nlen);
-  ti.kb_count = s.g_kb[lo];
-  if (MODE == MODE_FWD) {
-    ti.klen = g.k_fwd;
-    ti.k0 = 0;
-    ti.a_row = lo * g.n_out + ti.mb * kBM;
-    ti.b_row = s.g_start[lo] + ti.n0;
-  } else {
-    ti.klen = s.g_len[lo];
-    ti.k0 = s.g_start[lo];
-    ti.a_row = ti.mb * kBM;
-    ti.b_row = ti.n0;
-  }
-  ti.sfa0 = s.g_asf[lo] + ti.mb * ti.kb_count;
-  ti.sfb0 = s.g_bsf[lo] + ti.nt * ti.kb_count;
-  return ti;
-}
+struct TileWalker {
+  int e = -1, ts = 0, te = 0, nt_count = 1, q = 0, r = 0, kb = 0, gstart = 0, glen = 0, asf = 0,
+      bsf = 0, ext = 0;
 
-// decode_tile for a whole warp, every field broadcast from lane 0 so the
-// compiler can keep tile coordinates in uniform registers.
-template <int MODE>
-__device__ __forceinline__ TileInfo decode_tile_warp(const SmemLayout& s, const GemmArgs& g, int t,
-                                                     int rank) {
-  TileInfo ti = decode_tile<MODE>(s, g, t, rank);
-  ti.e = __shfl_sync(0xffffffffu, ti.e, 0);
-  ti.mb = __shfl_sync(0xffffffffu, ti.mb, 0);
-  ti.nt = __shfl_sync(0xffffffffu, ti.nt, 0);
-  ti.n0 = __shfl_sync(0xffffffffu, ti.n0, 0);
-  ti.nlen = __shfl_sync(0xffffffffu, ti.nlen, 0);
-  ti.kb_count = __shfl_sync(0xffffffffu, ti.kb_count, 0);
-  ti.klen = __shfl_sync(0xffffffffu, ti.klen, 0);
-  ti.k0 = __shfl_sync(0xffffffffu, ti.k0, 0);
-  ti.a_row = __shfl_sync(0xffffffffu, ti.a_row, 0);
-  ti.b_row = __shfl_sync(0xffffffffu, ti.b_row, 0);
-  ti.sfa0 = __shfl_sync(0xffffffffu, ti.sfa0, 0);
-  ti.sfb0 = __shfl_sync(0xffffffffu, ti.sfb0, 0);
-  return ti;
-}
+  template <class SL>
+  __device__ __forceinline__ void enter(const SL& s, const GemmArgs& g, int grp) {
+    e = grp;
+    ts = s.tile_start[grp];
+    te = s.tile_start[grp + 1];
+    const MetaView mv{const_cast<int*>(g.meta), g.E};
+    nt_count = max(__ldg(mv.g_nt() + grp), 1);
+    gstart = __ldg(mv.g_start() + grp);
+    glen = __ldg(mv.g_len() + grp);
+    kb = __ldg(mv.g_kb() + grp);
+    asf = __ldg(mv.g_asf() + grp);
+    bsf = __ldg(mv.g_bsf() + grp);
+    ext = MODE == MODE_FWD ? glen : g.n_ext;
+    const int units = (ext + 15) / 16;  // split_rows' balanced split, per group
+    q = units / nt_count;
+    r = units - q * nt_count;
+  }
+
+  template <class SL>
+  __device__ __forceinline__ TileInfo at(const SL& s, const GemmArgs& g, int t, int rank) {
+    if (e < 0 || t < ts) {
+      int lo = 0, hi = g.E - 1;  // last group whose first tile is <= t
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s.tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+      }
+      enter(s, g, lo);
+    }
+    while (t >= te) enter(s, g, e + 1);  // groups without tiles are passed over
+    TileInfo ti;
+    ti.e = e;
+    const int local = t - ts;
+    const int mbp = local / nt_count;
+    ti.nt = local - mbp * nt_count;
+    ti.mb = 2 * mbp + rank;
+    const int u0 = ti.nt * q + min(ti.nt, r);
+    const int ul = q + (ti.nt < r ? 1 : 0);
+    ti.n0 = 16 * u0;
+    ti.nlen = min(16 * ul, ext - ti.n0);
+    ti.kb_count = kb;
+    if (MODE == MODE_FWD) {
+      ti.klen = g.k_fwd;
+      ti.k0 = 0;
+      ti.a_row = e * g.n_out + ti.mb * kBM;
+      ti.b_row = gstart + ti.n0;
+    } else {
+      ti.klen = glen;
+      ti.k0 = gstart;
+      ti.a_row = ti.mb * kBM;
+      ti.b_row = ti.n0;
+    }
+    ti.sfa0 = asf + ti.mb * ti.kb_count;
+    ti.sfb0 = bsf + ti.nt * ti.kb_count;
+    return ti;
+  }
+
+  // For a whole warp: every field broadcast from lane 0, so the compiler can
+  // keep tile coordinates in uniform registers.
+  template <class SL>
+  __device__ __forceinline__ TileInfo at_warp(const SL& s, const GemmArgs& g, int t, int rank) {
+    TileInfo ti = at(s, g, t, rank);
+    ti.e = __shfl_sync(0xffffffffu, ti.e, 0);
+    ti.mb = __shfl_sync(0xffffffffu, ti.mb, 0);
+    ti.nt = __shfl_sync(0xffffffffu, ti.nt, 0);
+    ti.n0 = __shfl_sync(0xffffffffu, ti.n0, 0);
+    ti.nlen = __shfl_sync(0xffffffffu, ti.nlen, 0);
+    ti.kb_count = __shfl_sync(0xffffffffu, ti.kb_count, 0);
+    ti.klen = __shfl_sync(0xffffffffu, ti.klen, 0);
+    ti.k0 = __shfl_sync(0xffffffffu, ti.k0, 0);
+    ti.a_row = __shfl_sync(0xffffffffu, ti.a_row, 0);
+    ti.b_row = __shfl_sync(0xffffffffu, ti.b_row, 0);
+    ti.sfa0 = __shfl_sync(0xffffffffu, ti.sfa0, 0);
+    ti.sfb0 = __shfl_sync(0xffffffffu, ti.sfb0, 0);
+    return ti;
+  }
+};
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -614,7 +677,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& g, const TileInfo& t
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmSFA,
@@ -623,25 +686,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmOut16,
                         const __grid_constant__ CUtensorMap tmOutAux, GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
-  SmemLayout& s = *reinterpret_cast<SmemLayout*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using SL = SmemOf<MODE>;
+  constexpr int kStages = Cfg<MODE>::kStages, kEpiWarps = Cfg<MODE>::kEpiWarps;
+  constexpr int kThreads = Cfg<MODE>::kThreads;
+  SL& s = *reinterpret_cast<SL*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = int(cluster_ctarank());
   const int pair = int(cluster_id_x());
   const int npairs = int(num_clusters_x());
 
   MetaView mv{const_cast<int*>(g.meta), g.E};
-  for (int i = threadIdx.x; i <= g.E; i += kThreads) {
-    s.tile_start[i] = mv.tile_start()[i];
-    s.g_asf[i] = mv.g_asf()[i];
-    s.g_bsf[i] = mv.g_bsf()[i];
-  }
-  for (int i = threadIdx.x; i < g.E; i += kThreads) {
-    s.g_start[i] = mv.g_start()[i];
-    s.g_len[i] = mv.g_len()[i];
-    s.g_nt[i] = mv.g_nt()[i];
-    s.g_kb[i] = mv.g_kb()[i];
-  }
+  for (int i = threadIdx.x; i <= g.E; i += kThreads) s.tile_start[i] = mv.tile_start()[i];
   if (threadIdx.x == 0) {
     s.num_tiles = g.meta[0];
     s.abort_flag = 0;
@@ -653,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&s.acc_full[i]), 1);
-      mbar_init(smem_u32(&s.acc_empty[i]), 2 * 4);  // one arrival per epilogue warp, both CTAs
+      mbar_init(smem_u32(&s.acc_empty[i]), 2 * kEpiWarps);  // one arrival per epilogue warp, both CTAs
     }
     mbar_init(smem_u32(&s.drain), 1);
     mbar_init(smem_u32(&s.never), 1);
@@ -681,8 +736,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // elected lane issues the copies.
     uint32_t stage = 0, phase = 0, armed = 0, armed_par = 0;
     bool ok = true;
+    TileWalker<MODE> walk;
     for (int t = pair; t < num_tiles && ok; t += npairs) {
-      const TileInfo ti = decode_tile_warp<MODE>(s, g, t, rank);
+      const TileInfo ti = walk.at_warp(s, g, t, rank);
       const int half = int((uint32_t(ti.nlen + 15) & ~15u) >> 1);
       for (int kb = 0; kb < ti.kb_count; ++kb) {
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.empty[stage]), phase ^ 1u, wc))) {
@@ -691,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (elect_one_sync()) {
           const uint32_t fb_local = smem_u32(&s.full[stage]);
-          if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kStageTxPerCta);
+          if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * Cfg<MODE>::kStageTxPerCta);
           const uint32_t fb = mapa_shared(fb_local, 0);
           const int x = ti.k0 + kb * kBK;
           tma_load_2d_pair(smem_u32(s.a[stage]), &tmA, x, ti.a_row, fb);
@@ -721,8 +777,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0, sf_buf = 0;
       bool ok = true, issued = false;
       if (g.stall_test) ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s.never), 0, wc));
+      TileWalker<MODE> walk;
       for (int t = pair; t < num_tiles && ok; t += npairs) {
-        const TileInfo ti = decode_tile_warp<MODE>(s, g, t, 0);
+        const TileInfo ti = walk.at_warp(s, g, t, 0);
         if (ti.kb_count == 0) continue;
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s.acc_empty[acc]), acc_phase ^ 1u, wc))) {
           ok = false;
@@ -800,15 +857,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 0-3, both CTAs)
+    // ------------------------------------------------------------ epilogue (both CTAs)
     // TMEM loads are software-pipelined one 32-column chunk ahead; staged
     // chunks leave through TMA stores from two 2 KiB slots per warp, so the
     // next chunk is written while the previous store still reads its slot.
-    const int row = warp * 32 + lane;
+    // A warp reads TMEM lane quarter warp % 4 (the hardware's rule); with
+    // eight epilogue warps, warps 0-3 take the first half of a tile's
+    // 32-column chunks and warps 6-9 the second.
+    const int qw = warp & 3;                       // TMEM lane quarter = rows qw*32 .. qw*32+31
+    const int ew = warp < 4 ? warp : warp - 2;     // epilogue warp index (staging buffer)
+    const int grp = warp < 4 ? 0 : 1;              // column half (eight epilogue warps)
+    const int row = qw * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
-    uint32_t slot = 0;         // staging slot (2 KiB half of s.epi[warp]) the next store uses
+    uint32_t slot = 0;         // staging slot (2 KiB half of s.epi[ew]) the next store uses
     bool epi_pending = false;  // a TMA store of this warp may still read its staging buffer
-    uint8_t* const epi = s.epi[warp];
+    uint8_t* const epi = s.epi[ew];
+    // this warp's 32-column chunks [cb, ce) of a tile with nchunks chunks
+    // (an even split point keeps the bf16 chunk pairs within one warp)
+    auto chunk_range = [&](int nchunks, int& cb, int& ce) {
+      cb = 0;
+      ce = nchunks;
+      if (kEpiWarps == 8) {
+        const int h = min(nchunks, (((nchunks + 1) >> 1) + 1) & ~1);
+        cb = grp ? h : 0;
+        ce = grp ? nchunks : h;
+      }
+    };
     const bool f32 = g.out_dtype == MXG_DTYPE_F32;
     // free the slot about to be written: at most the other slot's store may still read
     auto slot_ready = [&]() {
@@ -827,18 +901,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       epi_pending = true;
     };
+    TileWalker<MODE> walk;
     for (int t = pair; t < num_tiles; t += npairs) {
-      const TileInfo ti = decode_tile<MODE>(s, g, t, rank);
+      const TileInfo ti = walk.at(s, g, t, rank);
       if (ti.kb_count == 0) {  // empty group (wgrad): dW[e] = 0
         uint32_t z[32];
-        for (int c0 = 0; c0 < ti.nlen; c0 += 32) store_chunk<MODE>(g, ti, row, c0, z, true);
+        int cb, ce;
+        chunk_range((ti.nlen + 31) >> 5, cb, ce);
+        for (int ci = cb; ci < ce; ++ci) store_chunk<MODE>(g, ti, row, 32 * ci, z, true);
         continue;
       }
       bool ok = mbar_wait(smem_u32(&s.acc_full[acc]), acc_phase, wc);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tb = tmem_base + (uint32_t(warp * 32) << 16) + acc * kAccStride;
+      const uint32_t tb = tmem_base + (uint32_t(qw * 32) << 16) + acc * kAccStride;
       const uint32_t acc_empty_leader = mapa_shared(smem_u32(&s.acc_empty[acc]), 0);
       auto release_acc = [&]() {  // accumulator fully read: let the next tile's MMAs start
         tc_fence_before();
@@ -850,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (MODE == MODE_FWD && g.fwd_tma_store && (cols_here == 32 || cols_here == 16)) {
           // this warp holds 32 features (lanes) x 32 tokens (columns): stage it
           // transposed as [token][feature] and store whole token rows
-          const int f0 = ti.mb * kBM + warp * 32;
+          const int f0 = ti.mb * kBM + qw * 32;
           if (f32) {  // 32 tokens x 128 B, 128-byte swizzle: the whole 4 KiB buffer
             if (epi_pending) {
               if (lane == 0) bulk_wait_group_read0();
@@ -879,7 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 64-byte swizzle) for the remainder of a 240-column tile; the
           // store clips at the tensor edge.  Half as many store requests as
           // 64-byte rows through two 2 KiB slots, which measured slower.
-          const int r0 = ti.mb * kBM + warp * 32;
+          const int r0 = ti.mb * kBM + qw * 32;
           if (epi_pending) {
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
@@ -904,7 +981,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // rows.  A chunk without a full partner (the tile's last 32 or 16
           // columns) leaves alone: 64-byte rows (64-byte swizzle) or 32-byte
           // rows (unswizzled); the tensor edge clips every store.
-          const int r0 = ti.mb * kBM + warp * 32;
+          const int r0 = ti.mb * kBM + qw * 32;
           const int pair0 = c0 & ~63;
           const bool paired = pair0 + 64 <= ti.nlen;
           auto pack8 = [&](int u) {
@@ -943,17 +1020,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_chunk<MODE>(g, ti, row, c0, v, false);
         }
       };
-      const int nchunks = (ti.nlen + 31) >> 5;
+      int cb, ce;
+      chunk_range((ti.nlen + 31) >> 5, cb, ce);
       uint32_t va[32], vb[32];
-      tmem_ld_32x32b_x32(tb, va);
-      for (int ci = 0; ci < nchunks; ci += 2) {
+      if (cb < ce) tmem_ld_32x32b_x32(tb + uint32_t(32 * cb), va);
+      else release_acc();  // no columns for this warp in this tile
+      for (int ci = cb; ci < ce; ci += 2) {
         tmem_ld_wait_regs(va);
-        if (ci + 1 < nchunks) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 1)), vb);
+        if (ci + 1 < ce) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 1)), vb);
         else release_acc();
         emit(32 * ci, va);
-        if (ci + 1 < nchunks) {
+        if (ci + 1 < ce) {
           tmem_ld_wait_regs(vb);
-          if (ci + 2 < nchunks) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 2)), va);
+          if (ci + 2 < ce) tmem_ld_32x32b_x32(tb + uint32_t(32 * (ci + 2)), va);
           else release_acc();
           emit(32 * (ci + 1), vb);
         }
@@ -1101,10 +1180,11 @@ static WsLayout ws_layout(int mode, int E, int64_t M, int64_t n_out, int64_t n_e
   if (mode == MODE_FWD) {
     const int64_t kb = (K + kBK - 1) / kBK;
     asf = int64_t(E) * mb2 * kb;
-    bsf = kb * ((M + int64_t(kBNMax - 1) * E) / kBNMax + 1);
+    const int64_t bn = bn_max(MODE_FWD);
+    bsf = kb * ((M + (bn - 1) * E) / bn + 1);
   } else {
     const int64_t kbs = (M + int64_t(kBK - 1) * E) / kBK + 1;
-    const int64_t nt = (n_ext + kBNMax - 1) / kBNMax;
+    const int64_t nt = (n_ext + bn_max(MODE_WGRAD) - 1) / bn_max(MODE_WGRAD);
     asf = mb2 * kbs;
     bsf = nt * kbs;
   }
@@ -1118,36 +1198,47 @@ static WsLayout ws_layout(int mode, int E, int64_t M, int64_t n_out, int64_t n_e
   return w;
 }
 
-// Per device: kernel attributes and the number of CTA pairs that fit at once.
-static int configure_kernels(int* pairs) {
+// Kernel attributes of one mode and the number of its CTA pairs that fit at once.
+template <int MODE>
+static int configure_mode(int* pairs) {
+  const size_t smem = smem_bytes<MODE>();
+  if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(smem)) != cudaSuccess)
+    return MXG_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * 74, 1, 1);
+  cfg.blockDim = dim3(Cfg<MODE>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_kernel<MODE>, &cfg) != cudaSuccess || n < 1)
+    return MXG_ERR_CUDA;
+  *pairs = n;
+  return MXG_OK;
+}
+
+// Per device and mode: the CTA pairs of a persistent launch (set up once).
+static int configure_kernels(int mode, int* pairs) {
   static std::mutex mu;
-  static int cached_pairs[64] = {0};
+  static int cached_pairs[64][2] = {{0}};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MXG_ERR_CUDA;
   std::lock_guard<std::mutex> lk(mu);
-  if (cached_pairs[dev] == 0) {
-    if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE_FWD>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(grouped_gemm_kernel<MODE_WGRAD>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes)) != cudaSuccess)
-      return MXG_ERR_CUDA;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * 74, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_kernel<MODE_FWD>, &cfg) != cudaSuccess || n < 1)
-      return MXG_ERR_CUDA;
-    cached_pairs[dev] = n;
+  if (cached_pairs[dev][0] == 0) {
+    int st = configure_mode<MODE_FWD>(&cached_pairs[dev][0]);
+    if (st == MXG_OK) st = configure_mode<MODE_WGRAD>(&cached_pairs[dev][1]);
+    if (st != MXG_OK) {
+      cached_pairs[dev][0] = 0;
+      return st;
+    }
   }
-  *pairs = cached_pairs[dev];
+  *pairs = cached_pairs[dev][mode == MODE_WGRAD ? 1 : 0];
   return MXG_OK;
 }
 
@@ -1215,7 +1306,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   int st = check_device();
   if (st) return st;
   int pairs = 0;
-  st = configure_kernels(&pairs);
+  st = configure_kernels(P.mode, &pairs);
   if (st) return st;
   const int limit = gemm_sm_limit();  // leave SMs to concurrent kernels (peer exchanges)
   if (limit > 0) pairs = std::max(1, std::min(pairs, limit / 2));
@@ -1226,7 +1317,8 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   CUtensorMap tmA, tmB, tmSFA, tmSFB;
   st = make_tmap(&tmA, a_ptr, a_rows, P.kc, kBM);
   if (st) return st;
-  st = make_tmap(&tmB, b_ptr, b_rows, P.kc, kBHalf);
+  st = make_tmap(&tmB, b_ptr, b_rows, P.kc,
+                 P.mode == MODE_FWD ? Cfg<MODE_FWD>::kBHalf : Cfg<MODE_WGRAD>::kBHalf);
   if (st) return st;
   st = make_sf_tmap(&tmSFA, wsb + L.sfa_off, std::max<int64_t>(L.sfa_chunks, 1), 1);
   if (st) return st;
@@ -1282,8 +1374,8 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(unsigned(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.blockDim = dim3(unsigned(P.mode == MODE_FWD ? Cfg<MODE_FWD>::kThreads : Cfg<MODE_WGRAD>::kThreads), 1, 1);
+  cfg.dynamicSmemBytes = P.mode == MODE_FWD ? smem_bytes<MODE_FWD>() : smem_bytes<MODE_WGRAD>();
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;

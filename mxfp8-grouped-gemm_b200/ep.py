@@ -135,6 +135,19 @@ class CudaP2POps:
                                             max_blocks, _lib.stream_ptr(src.device)),
                    "mxg_ep_return_p2p")
 
+    def copy_runs(self, src, runs, peer_host, dst_rows):
+        """Contiguous row runs (src_row, dst_row, rows, dst_buf: host int64/int32
+        arrays) from src to the buffers at peer_host addresses, on the copy
+        engines (current stream)."""
+        src = src.contiguous()
+        row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
+        s_row, d_row, n_rows, d_buf = runs
+        addrs = np.ascontiguousarray(peer_host, dtype=np.uint64)
+        _lib.check(self.L.mxg_copy_runs(src.data_ptr() if src.numel() else None, src.shape[0], row_bytes,
+                                        s_row.ctypes.data, d_row.ctypes.data, n_rows.ctypes.data,
+                                        d_buf.ctypes.data, s_row.size, addrs.ctypes.data, addrs.size,
+                                        dst_rows, _lib.stream_ptr(src.device)), "mxg_copy_runs")
+
     def zero_pad_rows(self, buf, back_rank):
         row_bytes = buf.element_size() * (buf[0].numel() if buf.shape[0] else 0)
         _lib.check(self.L.mxg_ep_zero_pad_rows(buf.data_ptr() if buf.numel() else None, row_bytes,
@@ -180,6 +193,7 @@ class PeerBuffer:
             ptrs.append(p.value)
             self.opened.append(p.value)
         self.ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.ptrs_host = np.array(ptrs, dtype=np.uint64)
         self.nbytes = nbytes
         self.local = torch.as_tensor(_CudaMem(self.own, nbytes), device=device)
 
@@ -252,6 +266,53 @@ def balanced_placement(expert_load, world: int, refine_iters: int = 2000) -> np.
     return slot
 
 
+def copy_run_tables(counts_all: np.ndarray, me: int, pad: int):
+    """Copy-engine runs of rank ``me`` from the gathered slot counts C
+    [world, E] (the layout of ``mxg_ep_p2p_plan``: slot s of rank s // E_local
+    holds the rows of every source rank in rank order, groups padded to
+    ``pad``).  Returns (dispatch, return) run tables, each (src_row, dst_row,
+    rows, dst_rank) of host arrays with empty runs dropped, ordered by
+    destination rank starting with me+1 (the ranks then write to different
+    peers at the same time):
+      dispatch: send positions [pref[me][s], pref[me][s+1]) of slot s (rows of
+                the send-order buffer) -> rows [dest_base[s] + pref[me][s], ..)
+                of rank s // E_local;
+      return:   padded rows [gs[s] + sum_{r'<r} C[r'][s], .. + C[r][s]) of local
+                slot s -> rows [pref[r][s], ..) of rank r's return buffer."""
+    C = np.asarray(counts_all, dtype=np.int64)
+    W, E = C.shape
+    El = E // W
+    pref = np.concatenate([np.zeros((W, 1), np.int64), np.cumsum(C, axis=1)], axis=1)
+    padded = (C.sum(0) + pad - 1) // pad * pad
+    gs = np.zeros(E, np.int64)
+    for d in range(W):
+        gs[d * El:(d + 1) * El] = np.concatenate([[0], np.cumsum(padded[d * El:(d + 1) * El])[:-1]])
+    before = np.concatenate([np.zeros((1, E), np.int64), np.cumsum(C, axis=0)[:-1]], axis=0)  # rows of ranks < r
+    order = [(me + i) % W for i in range(1, W + 1)]
+    d_rows, d_src, d_dst, d_rank = [], [], [], []
+    for d in order:
+        for s in range(d * El, (d + 1) * El):
+            c = C[me, s]
+            if c:
+                d_src.append(pref[me, s])
+                d_dst.append(gs[s] + before[me, s])
+                d_rows.append(c)
+                d_rank.append(d)
+    r_rows, r_src, r_dst, r_rank = [], [], [], []
+    for r in order:
+        for s in range(me * El, (me + 1) * El):
+            c = C[r, s]
+            if c:
+                r_src.append(gs[s] + before[r, s])
+                r_dst.append(pref[r, s])
+                r_rows.append(c)
+                r_rank.append(r)
+    i64 = lambda v: np.ascontiguousarray(v, dtype=np.int64)
+    i32 = lambda v: np.ascontiguousarray(v, dtype=np.int32)
+    return ((i64(d_src), i64(d_dst), i64(d_rows), i32(d_rank)),
+            (i64(r_src), i64(r_dst), i64(r_rows), i32(r_rank)))
+
+
 @dataclass
 class DispatchPlan:
     send_rows: torch.Tensor     # [n*k] token row of each send position
@@ -271,6 +332,10 @@ class DispatchPlan:
     back_rank: torch.Tensor | None = None    # [M_pad] home rank of each padded row (-1: padding)
     back_row: torch.Tensor | None = None     # [M_pad] send position on that rank
     ret_order: torch.Tensor | None = None    # [n_recv] real rows grouped by home rank, rotated
+    # copy-engine runs (host arrays: src_row, dst_row, rows, dst_rank), each
+    # list of runs ordered by destination rank starting with rank me+1
+    runs_dispatch: tuple | None = None       # send-order rows of each slot -> the owner's buffer
+    runs_return: tuple | None = None         # padded rows of each (local expert, source rank) -> home
 
 
 class ExpertParallel:
@@ -436,15 +501,33 @@ class ExpertParallel:
             C, self.rank, pad, m_pad, recv_rows)
         send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
         recv_splits = Ch[:, self.rank * El:(self.rank + 1) * El].sum(1).tolist()
+        runs_d, runs_r = copy_run_tables(Ch, self.rank, pad)
         plan = DispatchPlan(send_rows, slot_pos, send_splits, recv_splits, None, None,
                             group_rows, padded[self.rank].tolist(), recv_rows, n, k,
-                            slot_start, dest_base, back_rank, back_row, ret_order)
+                            slot_start, dest_base, back_rank, back_row, ret_order, runs_d, runs_r)
         return self.dispatch_like(x, plan, "x"), plan
 
-    def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy") -> torch.Tensor:
+    def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy",
+                      copy_engines: bool = False) -> torch.Tensor:
         """Rows of x [n, H'] moved along an existing plan (same routing).  With
         the p2p transport the result lives in the named receive buffer ("x" is
-        the one ``dispatch`` fills) until the next exchange into it."""
+        the one ``dispatch`` fills) until the next exchange into it.
+        copy_engines: gather the rows into send order here, then move each
+        slot's run with the copy engines (no SMs taken from kernels running
+        beside the exchange) instead of one SM kernel storing to the peers."""
+        if plan.back_rank is not None and copy_engines:
+            m_pad = plan.back_rank.numel()
+            buf = self.buffers[buffer]
+            rows, row_bytes = self.capacity[buffer]
+            if x.shape[0] and x.element_size() * x[0].numel() != row_bytes:
+                self._barrier(x.device)
+                raise ValueError("row size differs from the receive buffer's")
+            local = buf.view(m_pad, x)
+            self.p2p.zero_pad_rows(local, plan.back_rank)
+            send = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
+            self.p2p.copy_runs(send, plan.runs_dispatch, buf.ptrs_host, rows)
+            self._barrier(x.device)
+            return local
         if plan.back_rank is not None:
             m_pad = plan.back_rank.numel()
             buf = self.buffers[buffer]
@@ -469,12 +552,15 @@ class ExpertParallel:
         sum over each token's choices (weighted when weights [n, k] given)."""
         return self.combine_finish(self.combine_send(y_local, plan), plan, weights)
 
-    def combine_send(self, y_local: torch.Tensor, plan: DispatchPlan, buffer: str = "ret") -> torch.Tensor:
+    def combine_send(self, y_local: torch.Tensor, plan: DispatchPlan, buffer: str = "ret",
+                     copy_engines: bool = False) -> torch.Tensor:
         """First half of ``combine``: every result row back to its home rank.
         Returns this rank's rows in send order [n*k, H'] (with the p2p
         transport: a view of the named return buffer, valid until the next
         combine into it; every rank must use the same buffer names in the
-        same order, since a first use allocates collectively)."""
+        same order, since a first use allocates collectively).
+        copy_engines: the rows of each (local expert, source rank) pair are
+        contiguous on both sides, so each moves as one copy-engine run."""
         if plan.back_rank is not None:
             if buffer not in self.buffers:
                 self._ensure_ret(buffer, y_local.device)
@@ -483,8 +569,11 @@ class ExpertParallel:
             if y_local.shape[0] and y_local.element_size() * y_local[0].numel() != row_bytes:
                 self._barrier(y_local.device)   # as in dispatch_like: nobody waits for this rank
                 raise ValueError("combine rows must have the dispatched rows' size")
-            self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
-                         self.p2p_max_blocks)
+            if copy_engines:
+                self.p2p.copy_runs(y_local, plan.runs_return, buf.ptrs_host, rows)
+            else:
+                self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
+                             self.p2p_max_blocks)
             self._barrier(y_local.device)
             return buf.view(plan.n_tokens * plan.topk, y_local)
         back_buf = self.ops.gather(y_local, plan.back, plan.recv_rows)

@@ -50,14 +50,18 @@ class ExpertFFN:
 
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
-                 wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True):
+                 wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True,
+                 copy_engines: bool = False):
         """With a comm stream, the dy dispatch and the returns run beside the
         GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
         they do, and runs the peer copies only there.  wgrad_dtype is the
         weight gradients' dtype: bf16 by default, as the reference's wgrad
         returns them (``wgrad_fused.py:41``), or fp32.  compute_dx: also
         compute the gradient of the token inputs (the gate/up dgrad and its
-        return to the tokens' ranks)."""
+        return to the tokens' ranks).  copy_engines: with a comm stream and
+        the peer-memory transport, the dy dispatch and the returns move as
+        copy-engine runs (cudaMemcpyAsync) instead of SM kernels, so the
+        exchanges take no SMs from the GEMMs they run beside."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
@@ -83,6 +87,7 @@ class ExpertFFN:
             self.wgut = (q.view(E, H, 2 * I), s.view(E, H, 2 * I // 32))
             del wgut
         self.comm = comm_stream
+        self.ce = bool(copy_engines and comm_stream is not None)
         self.reserve = reserve_sms if comm_stream is not None else 0
         if self.reserve:
             self.ep.p2p_max_blocks = self.reserve
@@ -128,7 +133,7 @@ class ExpertFFN:
         if comm is not None:
             comm.wait_stream(main)
         with side():
-            dy_local = ep.dispatch_like(dy, plan)
+            dy_local = ep.dispatch_like(dy, plan, copy_engines=self.ce)
             dy_ready = torch.cuda.Event()
             dy_ready.record()
         if comm is None:
@@ -145,7 +150,7 @@ class ExpertFFN:
         if comm is not None:
             comm.wait_stream(main)
         with side():
-            ret = ep.combine_send(y_local, plan)
+            ret = ep.combine_send(y_local, plan, copy_engines=self.ce)
         if comm is None:
             self._mark("return_y")
         main.wait_event(dy_ready)
@@ -166,7 +171,7 @@ class ExpertFFN:
             if comm is not None:
                 comm.wait_stream(main)
             with side():
-                ret_dx = ep.combine_send(dx_local, plan, buffer="ret_dx")
+                ret_dx = ep.combine_send(dx_local, plan, buffer="ret_dx", copy_engines=self.ce)
             if comm is None:
                 self._mark("return_dx")
         with ops.gemm_sm_limit(self.gemm_sms):             # beside the dx return

@@ -217,3 +217,36 @@ def test_p2p_plan_places_rows_like_regroup(world):
                 assert np.array_equal(xs[r][routed[r][1][p]], out[d][0][q])
             else:
                 assert np.all(out[d][0][q] == 0)
+
+
+@pytest.mark.parametrize("world", [1, 3, 4])
+def test_copy_run_tables_place_rows_like_the_oracle(world):
+    """The copy-engine runs of every rank, applied on the host, put each
+    routed row where the oracle's regroup layout has it, and the return runs
+    bring every padded row's result back to its send position."""
+    from conftest import load_pkg
+    ep = load_pkg().ep
+    E, k, H = 4 * world, 3, 8
+    xs, ids = [], []
+    for r in range(world):
+        i, x, _ = make_rank_inputs(r, [40, 0, 77, 5][r], k, E, H, zipf=1.1)
+        xs.append(x), ids.append(i)
+    out, routed, _ = ep_oracle.simulate(xs, ids, E)
+    C = np.stack([rt[0] for rt in routed])
+    bufs = [np.zeros_like(o[0]) for o in out]
+    for r in range(world):
+        send = xs[r][routed[r][1]]
+        (src, dst, rows, rank), _ = ep.copy_run_tables(C, r, 32)
+        assert rows.min(initial=1) > 0 and rows.sum() == ids[r].size
+        for a, b, c, d in zip(src, dst, rows, rank):
+            bufs[d][b:b + c] = send[a:a + c]
+    for d in range(world):
+        assert np.array_equal(bufs[d], out[d][0])
+    for r in range(world):
+        back = np.full((ids[r].size, H), np.nan)
+        for d in range(world):
+            _, (src, dst, rows, rank) = ep.copy_run_tables(C, d, 32)
+            for a, b, c, q in zip(src, dst, rows, rank):
+                if q == r:
+                    back[b:b + c] = out[d][0][a:a + c]
+        assert np.array_equal(back, xs[r][routed[r][1]])

@@ -226,13 +226,13 @@ def test_p2p_dispatch_skips_unrouted_positions_and_bad_source_rows(mxg, cuda_dev
     assert routed == n * k - 3
     sr[routed:] = 1 << 30                       # garbage past the routed positions
     ok = (ids >= 0) & (ids < E)
-    want, _, _ = ep_oracle.simulate([x], [np.where(ok, ids, 0)], E)
+    xb = _bf16(x, cuda_dev)
+    want, _, _ = ep_oracle.simulate([xb.float().cpu().numpy()], [np.where(ok, ids, 0)], E)
     C = c.view(1, E)
     m_pad = int(((c.cpu().numpy() + 31) // 32 * 32).sum())
     pl = p2p.plan(C, 0, 32, m_pad, routed)
     buf = torch.zeros(m_pad + 8, H, dtype=torch.bfloat16, device=cuda_dev)
     ptrs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda_dev)
-    xb = _bf16(x, cuda_dev)
     p2p.dispatch(xb, sr, pl[0], pl[1], E, 0, ptrs, buf.shape[0])
     assert mxg.device_error() == 0
     # the oracle routed the bad slots to expert 0: compare the other experts' rows
