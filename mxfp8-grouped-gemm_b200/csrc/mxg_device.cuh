@@ -43,6 +43,22 @@ __device__ __forceinline__ uint32_t amax2(uint32_t w) {
   return a > b ? a : b;
 }
 
+// |x| bit patterns of both bf16 halves of a word, maxed per half with
+// another such pair (one SIMD max per two elements).  The bit patterns of
+// non-negative bf16 values order like the values; NaN patterns order above
+// +Inf, so a block holding a NaN keeps a NaN amax.
+__device__ __forceinline__ uint32_t abs2(uint32_t w) { return w & 0x7FFF7FFFu; }
+__device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) { return __vmaxu2(a, b); }
+
+// amax bit pattern of the 8 bf16 values of a 16-byte chunk, still as two halves
+__device__ __forceinline__ uint32_t amax_chunk2(uint4 v) {
+  return max2(max2(abs2(v.x), abs2(v.y)), max2(abs2(v.z), abs2(v.w)));
+}
+__device__ __forceinline__ uint32_t halves_max(uint32_t m2) {
+  const uint32_t a = m2 & 0xFFFFu, b = m2 >> 16;
+  return a > b ? a : b;
+}
+
 // NaN-carrying block (scale byte 0xFF): patch the NaN lanes so their codes
 // keep the input's sign, as torch's float8_e4m3fn cast does.
 __device__ __forceinline__ uint32_t fix_nan_byte(uint32_t code, uint32_t bf16bits) {

@@ -50,12 +50,10 @@ __global__ void __launch_bounds__(256) quant_rowwise_kernel(const uint4* __restr
 #pragma unroll
     for (int u = 0; u < kRowUnroll; ++u) {
       const int64_t i = i0 + int64_t(u) * stride + lane;
-      uint32_t m = amax2(v[u].x);
-      m = max(m, amax2(v[u].y));
-      m = max(m, amax2(v[u].z));
-      m = max(m, amax2(v[u].w));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      uint32_t m2 = amax_chunk2(v[u]);
+      m2 = max2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
+      m2 = max2(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
+      const uint32_t m = halves_max(m2);
       const uint32_t b = rceil_byte(m);
       const float f = descale_of(b);
       uint32_t c0 = cvt_e4m3x2(bf16_lo(v[u].x) * f, bf16_hi(v[u].x) * f);
@@ -198,9 +196,10 @@ __device__ __forceinline__ void swiglu_grad_word(uint32_t g, uint32_t u, uint32_
 // block must call this together.
 __device__ __forceinline__ void encode_row_chunk(const DualArgs& a, uint4 v, int64_t row,
                                                  int64_t col, bool valid) {
-  uint32_t m = max(max(amax2(v.x), amax2(v.y)), max(amax2(v.z), amax2(v.w)));
-  m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  uint32_t m2 = amax_chunk2(v);
+  m2 = max2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
+  m2 = max2(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
+  const uint32_t m = halves_max(m2);
   const uint32_t b = rceil_byte(m);
   const float f = descale_of(b);
   uint32_t c0 = cvt_e4m3x2(bf16_lo(v.x) * f, bf16_hi(v.x) * f);
@@ -260,15 +259,14 @@ __device__ __forceinline__ void dual_column_pass(const DualArgs& a, const uint32
     // (the partner lane always has the same rblk and pcol: same predicate)
     const uint32_t* colp = &tile[32 * rblk + 16 * h][SWZ ? (pcol ^ (h << 4)) : pcol];
     uint32_t w[16];
-    uint32_t m0 = 0, m1 = 0;
+    uint32_t m2 = 0;  // amax bit patterns of the two columns, one per half
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       w[r] = colp[r * CW];
-      m0 = max(m0, w[r] & 0x7FFFu);
-      m1 = max(m1, (w[r] >> 16) & 0x7FFFu);
+      m2 = max2(m2, abs2(w[r]));
     }
-    m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-    m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+    m2 = max2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
+    const uint32_t m0 = m2 & 0xFFFFu, m1 = m2 >> 16;
     if (!row_ok || !col_ok) continue;
     const uint32_t b0 = rceil_byte(m0), b1 = rceil_byte(m1);
     const float f0 = descale_of(b0), f1 = descale_of(b1);
