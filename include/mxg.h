@@ -117,6 +117,23 @@ MXG_API int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups, in
                                 int64_t k, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* Run half of the grouped forward (after mxg_grouped_fwd_prepare) whose bf16
+ * output rows leave for other buffers instead of `out`: row q goes to row
+ * back_row[q] of dst_bufs[back_rank[q]] (dst_bufs: device array of n_dst
+ * buffer addresses, this GPU's or peers' -- mxg_peer_open; back_rank[q] < 0
+ * drops the row), row stride n elements.  This is the expert-parallel
+ * combine's return written from the epilogue of the GEMM that produces the
+ * rows, by plain stores, so the exchange overlaps the tensor-core work (the
+ * reference returns rows with a separate all-to-all after the GEMM,
+ * port_mxfp8.py:74,240).  n % 8 == 0; buffers 16-byte aligned; a
+ * destination row outside [0, dst_rows) is skipped and sets the device error
+ * word.  The caller orders the ranks around it as around mxg_ep_return_p2p. */
+MXG_API int mxg_grouped_fwd_run_scatter(const void* a, const void* w, int num_groups, int64_t m,
+                                        int64_t n, int64_t k, const uint64_t* dst_bufs, int n_dst,
+                                        const int32_t* back_rank, const int32_t* back_row,
+                                        int64_t dst_rows, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* Grouped forward for callers that cannot allocate device memory (a plugin
  * inside a framework that owns the device memory pool, or host code that must
  * not call cudaMalloc): same arguments and result as mxg_grouped_fwd, minus

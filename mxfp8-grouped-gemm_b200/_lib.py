@@ -46,6 +46,8 @@ _PROTOS = {
                                          _c_i64, _vp, _c_size, _vp]),
     "mxg_grouped_fwd_run": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,
                                      _c_size, _vp]),
+    "mxg_grouped_fwd_run_scatter": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,
+                                             _vp, _c_i64, _vp, _c_size, _vp]),
     "mxg_grouped_wgrad_prepare": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
                                            _c_i64, _vp, _c_size, _vp]),
     "mxg_grouped_wgrad_run": (_c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _c_int, _vp,

@@ -476,6 +476,14 @@ struct GemmArgs {
   int stall_test;
   int fwd_tma_store;    // forward output row stride is 16-byte aligned: store via TMA
   int wgrad_tma_store;  // wgrad output row stride is 16-byte aligned: store via TMA
+  // forward, bf16, scatter mode (non-null scatter_bufs): output row q leaves
+  // for row back_row[q] of buffer scatter_bufs[back_rank[q]] (this GPU's or
+  // a peer's memory, plain stores), nothing is written to `out`
+  const uint64_t* scatter_bufs;
+  const int32_t* back_rank;
+  const int32_t* back_row;
+  int scatter_nbufs;
+  int64_t scatter_rows;
 };
 
 template <int S, int EW, int BB>
@@ -924,7 +932,39 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       };
       auto emit = [&](int c0, const uint32_t (&v)[32]) {
         const int cols_here = min(32, ti.nlen - c0);
-        if (MODE == MODE_FWD && g.fwd_tma_store && (cols_here == 32 || cols_here == 16)) {
+        if (MODE == MODE_FWD && g.scatter_bufs != nullptr) {
+          // the [token][feature] staging of the bf16 path below, then every
+          // lane reads one 16-byte piece (8 features) of a token row and
+          // stores it straight into the row's home buffer: four lanes write
+          // one token's 64 bytes, eight tokens per instruction.  The reads
+          // are synchronous, so one 2 KiB slot suffices.
+          const int f0 = ti.mb * kBM + qw * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            *reinterpret_cast<__nv_bfloat16*>(epi + j * 64 + (((lane >> 3) ^ ((j >> 1) & 3)) * 16) +
+                                              (lane & 7) * 2) = __float2bfloat16_rn(__uint_as_float(v[j]));
+          __syncwarp();
+          const int p = lane & 3;
+          const int f = f0 + 8 * p;
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int j = it * 8 + (lane >> 2);
+            if (j < cols_here && f < g.n_out) {
+              const int64_t q = int64_t(ti.b_row) + c0 + j;
+              const int r = __ldg(g.back_rank + q);
+              if (r >= 0) {
+                const int64_t dr = __ldg(g.back_row + q);
+                const uint4 piece = *reinterpret_cast<const uint4*>(epi + j * 64 + ((p ^ ((j >> 1) & 3)) * 16));
+                if (r < g.scatter_nbufs && dr >= 0 && dr < g.scatter_rows)
+                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(g.scatter_bufs[r]) + dr * g.ldo + f) =
+                      piece;
+                else
+                  atomicCAS(g.err, 0, MXG_ERR_WORKSPACE_TOO_SMALL);
+              }
+            }
+          }
+          __syncwarp();  // the slot is rewritten by the next chunk
+        } else if (MODE == MODE_FWD && g.fwd_tma_store && (cols_here == 32 || cols_here == 16)) {
           // this warp holds 32 features (lanes) x 32 tokens (columns): stage it
           // transposed as [token][feature] and store whole token rows
           const int f0 = ti.mb * kBM + qw * 32;
@@ -1042,6 +1082,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     }
     if (epi_pending && lane == 0) bulk_wait_group0();
     __syncwarp();
+    if (MODE == MODE_FWD && g.scatter_bufs != nullptr) __threadfence_system();  // rows to peers
   }
 
   if (s.abort_flag) {  // unwinding: give copies issued by either CTA time to land
@@ -1298,9 +1339,18 @@ static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
   return cuda_status(cudaGetLastError());
 }
 
+// Destinations of a forward in scatter mode (see GemmArgs); null: write `out`.
+struct Scatter {
+  const uint64_t* bufs;
+  int nbufs;
+  const int32_t* back_rank;
+  const int32_t* back_row;
+  int64_t rows;
+};
+
 static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, const void* b_ptr,
                        int64_t b_rows, void* out, int out_dtype, int64_t ldo, void* ws,
-                       size_t ws_bytes, cudaStream_t stream) {
+                       size_t ws_bytes, cudaStream_t stream, const Scatter* scatter = nullptr) {
   const WsLayout L = ws_layout(P.mode, P.E, P.M, P.n_out, P.n_ext, P.kc);
   if (ws_bytes < L.total) return MXG_ERR_WORKSPACE_TOO_SMALL;
   int st = check_device();
@@ -1344,7 +1394,8 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
     }
   }
   // TMA stores need the output row stride (N elements) to be a multiple of 16 bytes
-  const bool fwd_tma = P.mode == MODE_FWD && (P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2)) % 16 == 0;
+  const bool fwd_tma = P.mode == MODE_FWD && scatter == nullptr &&
+                       (P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2)) % 16 == 0;
   if (fwd_tma) {
     st = make_out_tmap_fwd(&tmOut, out, P.M, P.n_out, out_dtype, 32);
     if (st) return st;
@@ -1366,6 +1417,11 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   ga.stall_test = stall > 0 ? 1 : 0;
   ga.fwd_tma_store = fwd_tma ? 1 : 0;
   ga.wgrad_tma_store = wgrad_tma ? 1 : 0;
+  ga.scatter_bufs = scatter ? scatter->bufs : nullptr;
+  ga.back_rank = scatter ? scatter->back_rank : nullptr;
+  ga.back_row = scatter ? scatter->back_row : nullptr;
+  ga.scatter_nbufs = scatter ? scatter->nbufs : 0;
+  ga.scatter_rows = scatter ? scatter->rows : 0;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -1382,7 +1438,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   cudaError_t e;
   if (P.mode == MODE_FWD) {
     e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<MODE_FWD>, tmA, tmB, tmSFA, tmSFB, tmOut, tmOut16, tmOutAux, ga);
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && scatter == nullptr) {
       const int64_t row_bytes = P.n_out * (out_dtype == MXG_DTYPE_F32 ? 4 : 2);
       zero_tail_kernel<<<num_sms(), 256, 0, stream>>>(meta, reinterpret_cast<uint8_t*>(out), P.M,
                                                       row_bytes);
@@ -1486,6 +1542,26 @@ extern "C" int mxg_grouped_fwd_run(const void* a, const void* w, int num_groups,
   const Problem P{MODE_FWD, num_groups, m, n, 0, k};
   return run_grouped(P, w, int64_t(num_groups) * n, a, m, out, out_dtype, n, workspace,
                      workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int mxg_grouped_fwd_run_scatter(const void* a, const void* w, int num_groups, int64_t m,
+                                           int64_t n, int64_t k, const uint64_t* dst_bufs, int n_dst,
+                                           const int32_t* back_rank, const int32_t* back_row,
+                                           int64_t dst_rows, void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+  int st = check_common(num_groups, m, n, k, MXG_DTYPE_BF16, kOffsGivenToPrepare, num_groups,
+                        MXG_OFFS_SIZES);
+  if (st) return st;
+  if (k % 32 != 0 || n % 8 != 0) return MXG_ERR_BAD_SHAPE;
+  if (n_dst < 1 || dst_rows < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if (m == 0) return MXG_OK;
+  if (!a || !w || !workspace || !dst_bufs || !back_rank || !back_row) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w) || !aligned16(workspace)) return MXG_ERR_MISALIGNED;
+  if (int64_t(num_groups) * n > INT32_MAX) return MXG_ERR_BAD_SHAPE;
+  const Problem P{MODE_FWD, num_groups, m, n, 0, k};
+  const Scatter sc{dst_bufs, n_dst, back_rank, back_row, dst_rows};
+  return run_grouped(P, w, int64_t(num_groups) * n, a, m, nullptr, MXG_DTYPE_BF16, n, workspace,
+                     workspace_bytes, (cudaStream_t)stream, &sc);
 }
 
 extern "C" int mxg_grouped_wgrad(const void* go, const void* go_scales, const void* ia,

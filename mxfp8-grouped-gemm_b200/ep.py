@@ -579,6 +579,28 @@ class ExpertParallel:
         back_buf = self.ops.gather(y_local, plan.back, plan.recv_rows)
         return self._a2a(back_buf, plan.n_tokens * plan.topk, plan.send_splits, plan.recv_splits)
 
+    def return_target(self, plan: DispatchPlan, like: torch.Tensor, buffer: str = "ret"):
+        """Where a kernel that produces this rank's result rows (in the
+        dispatch layout) stores them so that they land at home: (device array
+        of every rank's address of the named return buffer, back_rank,
+        back_row, capacity rows).  Peer-memory transport only.  The producer
+        is followed by ``return_done``."""
+        if plan.back_rank is None:
+            raise ValueError("return_target needs the peer-memory transport")
+        if buffer not in self.buffers:
+            self._ensure_ret(buffer, like.device)
+        rows, row_bytes = self.capacity[buffer]
+        if like.element_size() * int(np.prod(like.shape[1:])) != row_bytes:
+            raise ValueError("result rows must have the dispatched rows' size")
+        return self.buffers[buffer].ptrs, plan.back_rank, plan.back_row, rows
+
+    def return_done(self, plan: DispatchPlan, like: torch.Tensor, buffer: str = "ret") -> torch.Tensor:
+        """After the producer of ``return_target``: every rank's rows have
+        landed; this rank's rows in send order [n*k, H'] (a view of the return
+        buffer, as ``combine_send`` returns)."""
+        self._barrier(like.device)
+        return self.buffers[buffer].view(plan.n_tokens * plan.topk, like)
+
     def combine_finish(self, ret: torch.Tensor, plan: DispatchPlan, weights=None) -> torch.Tensor:
         """Second half of ``combine``: the weighted sum over each token's choices."""
         return self.ops.combine(ret, plan.slot_pos, weights, plan.n_tokens, plan.topk)

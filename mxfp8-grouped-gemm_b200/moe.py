@@ -51,7 +51,7 @@ class ExpertFFN:
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
                  wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True,
-                 copy_engines: bool = False):
+                 copy_engines: bool = False, fused_return: bool = True):
         """With a comm stream, the dy dispatch and the returns run beside the
         GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
         they do, and runs the peer copies only there.  wgrad_dtype is the
@@ -61,7 +61,10 @@ class ExpertFFN:
         return to the tokens' ranks).  copy_engines: with a comm stream and
         the peer-memory transport, the dy dispatch and the returns move as
         copy-engine runs (cudaMemcpyAsync) instead of SM kernels, so the
-        exchanges take no SMs from the GEMMs they run beside."""
+        exchanges take no SMs from the GEMMs they run beside.  fused_return:
+        with the peer-memory transport, the down projection and the gate/up
+        dgrad store their result rows straight into the tokens' home ranks
+        from their epilogues (no local result tensor, no separate return)."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
@@ -88,6 +91,7 @@ class ExpertFFN:
             del wgut
         self.comm = comm_stream
         self.ce = bool(copy_engines and comm_stream is not None)
+        self.fused_return = bool(fused_return and ep.transport == "p2p")
         self.reserve = reserve_sms if comm_stream is not None else 0
         if self.reserve:
             self.ep.p2p_max_blocks = self.reserve
@@ -109,6 +113,16 @@ class ExpertFFN:
         wq, ws = w
         return ops.grouped_fwd(q, wq, offs, s, ws, out_dtype=out_dtype, offs_kind=_lib.OFFS_SIZES)
 
+    def _fwd_home(self, a, w, offs, like, buffer):
+        """Grouped forward whose result rows go straight to their home ranks'
+        return buffer (the combine's return from the epilogue)."""
+        q, s = a
+        wq, ws = w
+        bufs, back_rank, back_row, rows = self.ep.return_target(self._plan, like, buffer)
+        fp = ops.GroupedFwdPlan(s, ws, offs, wq.shape[0], q.shape[0], wq.shape[1], q.shape[1], q.device,
+                                offs_kind=_lib.OFFS_SIZES)
+        fp.run_scatter(q, wq, bufs, back_rank, back_row, rows)
+
     def _wgrad(self, go, ia, offs):
         return ops.grouped_wgrad(go[0], ia[0], offs, go[1], ia[1], out_dtype=self.wgrad_dtype,
                                  offs_kind=_lib.OFFS_SIZES, num_groups=self.E)
@@ -128,6 +142,7 @@ class ExpertFFN:
         side = (lambda: torch.cuda.stream(comm)) if comm is not None else nullcontext
         self._mark("start")
         x_local, plan = ep.dispatch(x, expert_ids)
+        self._plan = plan
         offs = plan.group_rows
         self._mark("dispatch_x")
         if comm is not None:
@@ -145,14 +160,21 @@ class ExpertFFN:
         self._mark("fwd_gate_up")
         hq, hs, ia_d, ias_d = ops.swiglu_quantize(gu)        # h is never written in bf16
         self._mark("swiglu_quantize_h")
-        y_local = self._fwd((hq, hs), self.wd, offs)
-        self._mark("fwd_down")
-        if comm is not None:
-            comm.wait_stream(main)
-        with side():
-            ret = ep.combine_send(y_local, plan, copy_engines=self.ce)
-        if comm is None:
+        y_local = None
+        if self.fused_return:                               # down projection -> home ranks
+            self._fwd_home((hq, hs), self.wd, offs, x, "ret")
+            self._mark("fwd_down")
+            ret = ep.return_done(plan, x, "ret")
             self._mark("return_y")
+        else:
+            y_local = self._fwd((hq, hs), self.wd, offs)
+            self._mark("fwd_down")
+            if comm is not None:
+                comm.wait_stream(main)
+            with side():
+                ret = ep.combine_send(y_local, plan, copy_engines=self.ce)
+            if comm is None:
+                self._mark("return_y")
         main.wait_event(dy_ready)
         dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
         self._mark("quantize_dy")
@@ -164,7 +186,12 @@ class ExpertFFN:
         dgq, dgs, go_g, gos_g = ops.swiglu_bwd_quantize(gu, dh, rowwise=self.compute_dx)
         self._mark("swiglu_bwd_quantize")                  # dgu is never written in bf16
         ret_dx = dx_local = None
-        if self.compute_dx:
+        if self.compute_dx and self.fused_return:          # gate/up dgrad -> home ranks
+            self._fwd_home((dgq, dgs), self.wgut, offs, x, "ret_dx")
+            self._mark("dgrad_gate_up")
+            ret_dx = ep.return_done(plan, x, "ret_dx")
+            self._mark("return_dx")
+        elif self.compute_dx:
             with ops.gemm_sm_limit(self.gemm_sms):
                 dx_local = self._fwd((dgq, dgs), self.wgut, offs)
             self._mark("dgrad_gate_up")
@@ -186,6 +213,10 @@ class ExpertFFN:
         dx = ep.combine_finish(ret_dx, plan, None) if ret_dx is not None else None
         self._mark("combine")
         if self.trace is not None:
+            if y_local is None:      # fused returns keep no local result: recompute it to check it
+                y_local = self._fwd((hq, hs), self.wd, offs)
+                if self.compute_dx:
+                    dx_local = self._fwd((dgq, dgs), self.wgut, offs)
             self._keep(x_local=x_local.clone(), dy_local=dy_local.clone(), xq=xq, xs=xs, ia_g=ia_g,
                        ias_g=ias_g, gu=gu, hq=hq, hs=hs, ia_d=ia_d, ias_d=ias_d, y_local=y_local,
                        dyq=dyq, dys=dys, go_d=go_d, gos_d=gos_d, dh=dh, dgq=dgq, dgs=dgs, go_g=go_g,

@@ -308,6 +308,19 @@ class GroupedFwdPlan:
         return out
 
 
+    def run_scatter(self, a, w, dst_bufs, back_rank, back_row, dst_rows):
+        """The forward with its bf16 output rows stored into other buffers
+        (this GPU's or peers'): row q to row back_row[q] of the buffer at
+        address dst_bufs[back_rank[q]] (dst_bufs: int64 device tensor of
+        addresses; back_rank < 0 drops the row)."""
+        a = _operand(a, "a_fp8")
+        w = _operand(w, "w_fp8")
+        _lib.check(_lib.load().mxg_grouped_fwd_run_scatter(
+            a.data_ptr(), w.data_ptr(), self.E, self.M, self.N, self.K, dst_bufs.data_ptr(),
+            dst_bufs.numel(), back_rank.data_ptr(), back_row.data_ptr(), dst_rows, self.ws.data_ptr(),
+            self.ws.numel(), _lib.stream_ptr(a.device)), "mxg_grouped_fwd_run_scatter")
+
+
 class GroupedWgradPlan:
     """Groups and packed scales of one grouped weight gradient (the
     counterpart of the reference's wgrad_prepare, without operand copies)."""

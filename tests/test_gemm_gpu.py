@@ -133,6 +133,57 @@ def test_fwd_ragged(mxg, orc, cuda_dev, sizes, N, K):
     check_fwd(mxg, orc, a, w, offs, a_s, w_s, kind=0, out_dtype=torch.bfloat16)
 
 
+@pytest.mark.parametrize("sizes,N,K", [([300, 0, 517, 64, 1200], 384, 1024), ([96, 2048, 32], 7168, 2048)])
+def test_fwd_scatter_rows_land_like_the_regular_output(mxg, cuda_dev, sizes, N, K):
+    """The forward whose epilogue stores each output row into another buffer
+    (the expert-parallel return written from the GEMM): three destination
+    buffers on this GPU stand in for three ranks; every kept row equals the
+    regular forward's row bit for bit, dropped rows (back_rank -1) land
+    nowhere, and the untouched destination rows keep their fill."""
+    gen = torch.Generator(device=cuda_dev).manual_seed(N + K)
+    E, M = len(sizes), sum(sizes)
+    a, w = rand_codes((M, K), gen, cuda_dev), rand_codes((E, N, K), gen, cuda_dev)
+    a_s, w_s = rand_scales((M, K // 32), gen, cuda_dev), rand_scales((E, N, K // 32), gen, cuda_dev)
+    offs = torch.tensor(sizes, dtype=torch.int32, device=cuda_dev)
+    y = mxg.ops.grouped_fwd(a, w, offs, a_s, w_s, offs_kind=2)
+    rng = np.random.default_rng(7)
+    ranks = rng.integers(-1, 3, M).astype(np.int32)
+    cap = M + 16
+    rows = np.full(M, -1, np.int32)
+    for r in range(3):
+        idx = np.nonzero(ranks == r)[0]
+        rows[idx] = rng.permutation(cap)[:idx.size]
+    bufs = [torch.full((cap, N), 7.0, dtype=torch.bfloat16, device=cuda_dev) for _ in range(3)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=cuda_dev)
+    plan = mxg.ops.GroupedFwdPlan(a_s, w_s, offs, E, M, N, K, cuda_dev, offs_kind=2)
+    plan.run_scatter(a, w, ptrs, torch.from_numpy(ranks).to(cuda_dev), torch.from_numpy(rows).to(cuda_dev), cap)
+    assert mxg.device_error() == 0
+    yh = y.view(torch.int16).cpu().numpy()
+    for r in range(3):
+        got = bufs[r].view(torch.int16).cpu().numpy()
+        idx = np.nonzero(ranks == r)[0]
+        assert np.array_equal(got[rows[idx]], yh[idx])
+        untouched = np.setdiff1d(np.arange(cap), rows[idx])
+        assert np.all(bufs[r].float().cpu().numpy()[untouched] == 7.0)
+
+
+def test_fwd_scatter_rejects_rows_past_capacity(mxg, cuda_dev):
+    """A destination row outside its buffer is skipped and reported."""
+    gen = torch.Generator(device=cuda_dev).manual_seed(3)
+    E, M, N, K = 2, 64, 256, 256
+    a, w = rand_codes((M, K), gen, cuda_dev), rand_codes((E, N, K), gen, cuda_dev)
+    offs = torch.tensor([32, 32], dtype=torch.int32, device=cuda_dev)
+    buf = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda_dev)
+    guard = torch.zeros(64, N, dtype=torch.bfloat16, device=cuda_dev)
+    ptrs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=cuda_dev)
+    rows = torch.arange(M, dtype=torch.int32, device=cuda_dev)
+    rows[5] = M + 3
+    plan = mxg.ops.GroupedFwdPlan(None, None, offs, E, M, N, K, cuda_dev, offs_kind=2)
+    plan.run_scatter(a, w, ptrs, torch.zeros(M, dtype=torch.int32, device=cuda_dev), rows, M)
+    assert mxg.device_error() == mxg._lib.MXG_ERR_WORKSPACE_TOO_SMALL
+    assert torch.all(guard == 0)
+
+
 def test_fwd_uncovered_rows_are_zero(mxg, orc, cuda_dev):
     gen = torch.Generator(device=cuda_dev).manual_seed(5)
     M, N, K = 300, 128, 64
