@@ -659,7 +659,7 @@ class EpLayerBench:
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
                  transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16", experts=EP_EXPERTS,
-                 logp=None, compute_dx=True, copy_engines=False):
+                 logp=None, compute_dx=True, copy_engines=False, fused_return=True):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -687,7 +687,7 @@ class EpLayerBench:
         self.layer = m.moe.ExpertFFN(self.ep, w_gu, w_d, comm_stream=self.comm,
                                      wgrad_dtype=torch.float32 if wgrad_dtype == "fp32" else torch.bfloat16,
                                      reserve_sms=reserve_sms, compute_dx=compute_dx,
-                                     copy_engines=copy_engines)
+                                     copy_engines=copy_engines, fused_return=fused_return)
         del w_gu, w_d
         torch.cuda.synchronize()
 
@@ -963,7 +963,7 @@ def run_ep_mxg(args, rank, world, local):
     lb = EpLayerBench(rank, world, seed=args.seed, placement=args.placement, overlap=args.overlap,
                       transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
                       wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx,
-                      copy_engines=args.copy_engines)
+                      copy_engines=args.copy_engines, fused_return=not args.no_fused_return)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -996,7 +996,8 @@ def run_ep_mxg(args, rank, world, local):
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
            "data": "synthetic",
            "config": ep_config(world, args.placement, args.overlap, r["transport"], r["reserve_sms"],
-                               args.ep_wgrad_dtype, args.seed, not args.no_dx, args.copy_engines),
+                               args.ep_wgrad_dtype, args.seed, not args.no_dx, args.copy_engines,
+                               not args.no_fused_return),
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
                "padded_rows_this_rank", "segments_ms_rank0", "exchange_ms_rank0", "gemm_ms_rank0",
@@ -1034,7 +1035,8 @@ def ep_flops(rows, dx=True):
     return (18 if dx else 14) * int(rows) * HIDDEN * INTER
 
 
-def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx, copy_engines=False):
+def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx, copy_engines=False,
+              fused=True):
     """The config object of a config-4 line (the reference arm prints the same)."""
     rows, padded = ep_routing_stats(world, seed, placement)
     flops_rank = ep_flops(rows[0], dx)
@@ -1047,6 +1049,7 @@ def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, se
             "hidden": HIDDEN, "intermediate": INTER, "placement": placement,
             "comm_overlap": overlap, "transport": transport, "reserved_sms": reserve_sms,
             "exchange_engine": "copy engines" if (overlap and copy_engines) else "SM kernels",
+            "returns": "from the GEMM epilogues" if (fused and transport == "p2p") else "separate exchange",
             "dw_dtype": wgrad_dtype + (" (the reference's wgrad output dtype)" if wgrad_dtype == "bf16" else ""),
             "routed_rows_per_gpu": EP_TOKENS * EP_TOPK, "max_rows_received_per_gpu": rows_max,
             "padded_rows": padded,  # rank 0's
@@ -1259,7 +1262,7 @@ def run_reference_layer(args, world):
            "config": ep_config(world, args.placement, args.overlap,
                                "nccl" if args.transport == "nccl" else "p2p",
                                args.reserve_sms if args.overlap else 0, args.ep_wgrad_dtype, args.seed,
-                               not args.no_dx, args.copy_engines),
+                               not args.no_dx, args.copy_engines, not args.no_fused_return),
            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
                             "kind": "port", "sample": sample},
            "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1341,6 +1344,8 @@ def main():
     ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
                     help="weight-gradient dtype of the config-4 expert layer (bf16: the reference's "
                          "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
+    ap.add_argument("--no-fused-return", action="store_true",
+                    help="EP layer: return result rows with a separate exchange instead of from the GEMM epilogue")
     ap.add_argument("--copy-engines", action="store_true",
                     help="EP layer with --overlap: the dy dispatch and the returns as copy-engine runs")
     ap.add_argument("--no-dx", action="store_true",
