@@ -251,6 +251,38 @@ def test_p2p_dispatch_skips_unrouted_positions_and_bad_source_rows(mxg, cuda_dev
     assert torch.all(buf[m_pad:] == 0)
 
 
+def test_copy_runs_move_rows_and_refuse_out_of_bounds_runs(mxg, cuda_dev):
+    """mxg_copy_runs (copy-engine row runs) between buffers of this GPU: the
+    dispatch run tables of four emulated ranks put every row where the
+    oracle's layout has it; a run past a destination's end is refused before
+    any copy."""
+    world, E, k, H = 4, 16, 3, 64
+    ns = [300, 0, 517, 64]
+    ins = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
+    xs = [_bf16(a[1], cuda_dev) for a in ins]
+    out, routed, _ = ep_oracle.simulate([x.float().cpu().numpy() for x in xs], [a[0] for a in ins], E)
+    C = np.stack([rt[0] for rt in routed])
+    cap = max(o[0].shape[0] for o in out) + 5
+    bufs = [torch.zeros(cap, H, dtype=torch.bfloat16, device=cuda_dev) for _ in range(world)]
+    addrs = np.array([b.data_ptr() for b in bufs], dtype=np.uint64)
+    p2p = mxg.ep.CudaP2POps()
+    for r in range(world):
+        send = xs[r][torch.from_numpy(routed[r][1].astype(np.int64)).to(cuda_dev)]
+        runs, _ = mxg.ep.copy_run_tables(C, r, 32)
+        p2p.copy_runs(send, runs, addrs, cap)
+    torch.cuda.synchronize()
+    for d in range(world):
+        m_pad = out[d][0].shape[0]
+        assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), out[d][0])
+    src = torch.ones(8, H, dtype=torch.bfloat16, device=cuda_dev)
+    bad = (np.array([0], np.int64), np.array([cap - 4], np.int64), np.array([8], np.int64), np.array([0], np.int32))
+    before = bufs[0].clone()
+    with pytest.raises(mxg._lib.MxgError):
+        p2p.copy_runs(src, bad, addrs, cap)
+    torch.cuda.synchronize()
+    assert torch.equal(bufs[0], before)
+
+
 def _nccl_worker(rank, world, port, q, transport="nccl"):
     try:
         import datetime
