@@ -787,7 +787,9 @@ def measure_ep_layer(lb, world, steps, warmup):
             "recv_rows_per_rank": {"max": max(rows), "mean": sum(rows) / len(rows), "min": min(rows)},
             "padded_rows_this_rank": int(sum(plan.group_rows_host)),
             "segments_ms_rank0": {k: round(v, 4) for k, v in seg.items()},
-            "exchange_ms_rank0": round(sum(exch.values()), 4) if lb.comm is None else None,
+            # exchanges on the main stream's timeline (the x dispatch always; the
+            # dy dispatch and the returns only when they are not on the side stream)
+            "exposed_exchange_ms_rank0": round(sum(exch.values()), 4),
             "gemm_ms_rank0": round(sum(gemm_ms.values()), 4),
             "gemm_tflops_rank0": {k: round(flops[k] / (gemm_ms[k] * 1e-3) / 1e12, 1) for k in flops},
             "roofline": tensor_roofline(achieved, ms * steps * 1e-3, pk,
@@ -984,7 +986,7 @@ def run_ep_mxg(args, rank, world, local):
         verified["nccl"] = verify_ep_layer(lb2, world, rank, args.seed)
         other = {"transport": "nccl", "value": round(r2["value"], 2), "unit": "TFLOPS",
                  "ms_per_step": round(r2["ms_per_step"], 4), "steps": min(args.steps, 20),
-                 "segments_ms_rank0": r2["segments_ms_rank0"], "exchange_ms_rank0": r2["exchange_ms_rank0"],
+                 "segments_ms_rank0": r2["segments_ms_rank0"], "exposed_exchange_ms_rank0": r2["exposed_exchange_ms_rank0"],
                  "gemm_tflops_rank0": r2["gemm_tflops_rank0"],
                  "gpu_launches_per_step": EP_LAUNCHES_PER_STEP["nccl"]}
         lb2.close()
@@ -1000,7 +1002,7 @@ def run_ep_mxg(args, rank, world, local):
                                not args.no_fused_return),
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
-               "padded_rows_this_rank", "segments_ms_rank0", "exchange_ms_rank0", "gemm_ms_rank0",
+               "padded_rows_this_rank", "segments_ms_rank0", "exposed_exchange_ms_rank0", "gemm_ms_rank0",
                "gemm_tflops_rank0")},
            "layer_nccl": other, "verified": verified,
            "cpu_baseline": None, "e2e": e2e,
@@ -1333,9 +1335,10 @@ def main():
                     help="small: reduced problem for profiler captures (not a bench line)")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement for the EP layer (N>1)")
-    ap.add_argument("--overlap", action="store_true",
-                    help="EP layer: run the dy dispatch and the combine's return beside the GEMMs "
-                         "(measured slower on 8 B200s: the GEMMs lose more than the exchange hides)")
+    ap.add_argument("--exchange", default="ce", choices=["ce", "sm", "seq"],
+                    help="EP layer (N>1): ce = the dy dispatch and both returns on the copy engines on a "
+                         "side stream beside the GEMMs (default); sm = the same beside the GEMMs with SM "
+                         "copy kernels; seq = SM copy kernels between the GEMMs")
     ap.add_argument("--no-ep", action="store_true", help="N=1: skip the one-GPU EP layer measurement")
     ap.add_argument("--no-mixtral", action="store_true", help="N=1: skip the config-3 (Mixtral-shaped) measurement")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
@@ -1344,10 +1347,9 @@ def main():
     ap.add_argument("--ep-wgrad-dtype", default="bf16", choices=["bf16", "fp32"],
                     help="weight-gradient dtype of the config-4 expert layer (bf16: the reference's "
                          "wgrad output; the N=1 GEMM set keeps config 2's fp32)")
-    ap.add_argument("--no-fused-return", action="store_true",
-                    help="EP layer: return result rows with a separate exchange instead of from the GEMM epilogue")
-    ap.add_argument("--copy-engines", action="store_true",
-                    help="EP layer with --overlap: the dy dispatch and the returns as copy-engine runs")
+    ap.add_argument("--fused-return", action="store_true",
+                    help="EP layer: the down projection and the gate/up dgrad store their rows into the "
+                         "home ranks from the GEMM epilogue (measured slower than a separate exchange)")
     ap.add_argument("--no-dx", action="store_true",
                     help="EP layer: skip the gate/up dgrad (input gradient) and its return")
     ap.add_argument("--no-nccl-layer", action="store_true",
@@ -1358,6 +1360,9 @@ def main():
                     help="EP layer with --overlap: SMs kept free of GEMM blocks for the peer copies")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.overlap = args.exchange in ("ce", "sm")
+    args.copy_engines = args.exchange == "ce"
+    args.no_fused_return = not args.fused_return
     if args.fp8_peak:
         measure_fp8_peak(args)
         return

@@ -51,7 +51,7 @@ class ExpertFFN:
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
                  wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True,
-                 copy_engines: bool = False, fused_return: bool = True):
+                 copy_engines: bool = False, fused_return: bool = False):
         """With a comm stream, the dy dispatch and the returns run beside the
         GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
         they do, and runs the peer copies only there.  wgrad_dtype is the
@@ -64,7 +64,9 @@ class ExpertFFN:
         exchanges take no SMs from the GEMMs they run beside.  fused_return:
         with the peer-memory transport, the down projection and the gate/up
         dgrad store their result rows straight into the tokens' home ranks
-        from their epilogues (no local result tensor, no separate return)."""
+        from their epilogues (no local result tensor, no separate return;
+        measured slower than a separate return on 2 B200s: the epilogue's
+        64-byte peer stores hold the GEMM back)."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
