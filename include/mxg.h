@@ -295,6 +295,18 @@ MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t src_rows, int64_t row_b
                                 const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
                                 void* stream);
 
+/* mxg_ep_dispatch_p2p of src, and in the same pass row send_rows[p] of src2
+ * (same row size and row count as src) copied to row p of gather_out (this
+ * GPU's memory, n_send rows): the second tensor put in send order for a
+ * later exchange on the copy engines (mxg_copy_runs), while the first one is
+ * bound by NVLink.  Default grid. */
+MXG_API int mxg_ep_dispatch_p2p_gather(const void* src, int64_t src_rows, int64_t row_bytes,
+                                       const int32_t* send_rows, int64_t n_send,
+                                       const int32_t* slot_start, const int32_t* dest_base,
+                                       int num_slots, int e_local, int me, const uint64_t* peer_bufs,
+                                       int64_t capacity_rows, const void* src2, void* gather_out,
+                                       void* stream);
+
 /* Padded local rows q = ret_order[i] (i < n_rows) -> row back_row[q] of
  * peer_bufs[back_rank[q]] (skipped where back_rank < 0). */
 MXG_API int mxg_ep_return_p2p(const void* src, int64_t row_bytes, const int32_t* ret_order,

@@ -76,6 +76,8 @@ _PROTOS = {
                                  _vp, _vp, _vp, _vp, _c_size, _vp]),
     "mxg_ep_dispatch_p2p": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int,
                                      _c_int, _vp, _c_i64, _c_int, _vp]),
+    "mxg_ep_dispatch_p2p_gather": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int,
+                                            _c_int, _vp, _c_i64, _vp, _vp, _vp]),
     "mxg_ep_return_p2p": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_int, _c_i64, _c_int,
                                    _vp]),
     "mxg_ep_zero_pad_rows": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp]),

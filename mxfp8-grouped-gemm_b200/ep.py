@@ -125,6 +125,19 @@ class CudaP2POps:
                                               capacity_rows, max_blocks,
                                               _lib.stream_ptr(src.device)), "mxg_ep_dispatch_p2p")
 
+    def dispatch_gather(self, src, send_rows, slot_start, dest_base, e_local, me, peer_ptrs, capacity_rows,
+                        src2, gather_out):
+        """dispatch of src, and src2's rows put in send order into gather_out
+        in the same pass."""
+        src, src2 = src.contiguous(), src2.contiguous()
+        row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
+        _lib.check(self.L.mxg_ep_dispatch_p2p_gather(
+            src.data_ptr() if src.numel() else None, src.shape[0], row_bytes, send_rows.data_ptr(),
+            send_rows.numel(), slot_start.data_ptr(), dest_base.data_ptr(), dest_base.numel(), e_local, me,
+            peer_ptrs.data_ptr(), capacity_rows, src2.data_ptr() if src2.numel() else None,
+            gather_out.data_ptr() if gather_out.numel() else None, _lib.stream_ptr(src.device)),
+            "mxg_ep_dispatch_p2p_gather")
+
     def ret(self, src, ret_order, back_rank, back_row, peer_ptrs, capacity_rows, max_blocks=0):
         src = src.contiguous()
         row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
@@ -336,6 +349,8 @@ class DispatchPlan:
     # list of runs ordered by destination rank starting with rank me+1
     runs_dispatch: tuple | None = None       # send-order rows of each slot -> the owner's buffer
     runs_return: tuple | None = None         # padded rows of each (local expert, source rank) -> home
+    pregathered: torch.Tensor | None = None  # [n*k, H'] a second tensor already in send order
+    pregathered_src: torch.Tensor | None = None  # ... namely this one
 
 
 class ExpertParallel:
@@ -433,10 +448,13 @@ class ExpertParallel:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
         return out
 
-    def dispatch(self, x: torch.Tensor, expert_ids: torch.Tensor):
+    def dispatch(self, x: torch.Tensor, expert_ids: torch.Tensor, also_gather: torch.Tensor | None = None):
         """x [n, H] token rows, expert_ids [n, k] global expert of each choice.
         Returns (x_local [M_pad, H] expert-major 32-padded rows of this rank's
-        expert slots, plan)."""
+        expert slots, plan).  also_gather ([n, H] like x, peer-memory
+        transport): put its rows in send order in the same pass
+        (``plan.pregathered``), for a later ``dispatch_like(...,
+        copy_engines=True)`` of that tensor."""
         n, k = expert_ids.shape
         slot_map = None
         if self.placement is not None:
@@ -445,7 +463,7 @@ class ExpertParallel:
             slot_map = self.slot_of_expert
         counts, send_rows, slot_pos = self.ops.route(expert_ids, self.num_experts, slot_map)
         if self.transport == "p2p":
-            return self._dispatch_p2p(x, n, k, counts, send_rows, slot_pos)
+            return self._dispatch_p2p(x, n, k, counts, send_rows, slot_pos, also_gather)
         recv_counts = self._a2a(counts, counts.numel()).view(self.world, self.e_local)
         host = torch.cat([counts, recv_counts.reshape(-1)]).cpu().view(2, self.world, self.e_local)
         sc = host[0].sum(1).tolist()
@@ -460,7 +478,7 @@ class ExpertParallel:
                             n_recv, n, k)
         return self.dispatch_like(x, plan), plan
 
-    def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos):
+    def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos, also_gather=None):
         E, W, El, pad = self.num_experts, self.world, self.e_local, self.pad
         # every rank's slot counts plus its number of routing slots n*k: a
         # routing slot whose expert id is out of range is counted nowhere, and
@@ -505,6 +523,19 @@ class ExpertParallel:
         plan = DispatchPlan(send_rows, slot_pos, send_splits, recv_splits, None, None,
                             group_rows, padded[self.rank].tolist(), recv_rows, n, k,
                             slot_start, dest_base, back_rank, back_row, ret_order, runs_d, runs_r)
+        if also_gather is not None and tuple(also_gather.shape) == tuple(x.shape) \
+                and also_gather.dtype == x.dtype:
+            m_pad = plan.back_rank.numel()
+            buf = self.buffers["x"]
+            rows, _ = self.capacity["x"]
+            local = buf.view(m_pad, x)
+            self.p2p.zero_pad_rows(local, plan.back_rank)
+            send = torch.empty((n * k,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+            self.p2p.dispatch_gather(x, send_rows, slot_start, dest_base, El, self.rank, buf.ptrs, rows,
+                                     also_gather, send)
+            self._barrier(x.device)
+            plan.pregathered, plan.pregathered_src = send, also_gather
+            return local, plan
         return self.dispatch_like(x, plan, "x"), plan
 
     def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy",
@@ -524,7 +555,10 @@ class ExpertParallel:
                 raise ValueError("row size differs from the receive buffer's")
             local = buf.view(m_pad, x)
             self.p2p.zero_pad_rows(local, plan.back_rank)
-            send = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
+            send = plan.pregathered if plan.pregathered_src is x else None
+            if send is None:
+                send = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
+            plan.pregathered = plan.pregathered_src = None
             self.p2p.copy_runs(send, plan.runs_dispatch, buf.ptrs_host, rows)
             self._barrier(x.device)
             return local

@@ -143,7 +143,9 @@ class ExpertFFN:
         comm = self.comm
         side = (lambda: torch.cuda.stream(comm)) if comm is not None else nullcontext
         self._mark("start")
-        x_local, plan = ep.dispatch(x, expert_ids)
+        # with copy-engine exchanges, dy is put in send order during the x
+        # dispatch (that pass is bound by NVLink), not by a gather beside the GEMMs
+        x_local, plan = ep.dispatch(x, expert_ids, also_gather=dy if self.ce else None)
         self._plan = plan
         offs = plan.group_rows
         self._mark("dispatch_x")
