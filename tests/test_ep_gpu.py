@@ -251,6 +251,36 @@ def test_p2p_dispatch_skips_unrouted_positions_and_bad_source_rows(mxg, cuda_dev
     assert torch.all(buf[m_pad:] == 0)
 
 
+def test_p2p_dispatch_gather_moves_rows_and_orders_the_second_tensor(mxg, cuda_dev):
+    """mxg_ep_dispatch_p2p_gather with four ranks emulated on one GPU: the
+    first tensor lands exactly as mxg_ep_dispatch_p2p puts it (the oracle's
+    layout), the second comes out in send order (src2[send_rows])."""
+    world, E, k, H = 4, 16, 3, 64
+    ns = [300, 0, 517, 64]
+    ins = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
+    xs = [_bf16(a[1], cuda_dev) for a in ins]
+    ys = [_bf16(a[1] * -3.0 + 1.0, cuda_dev) for a in ins]
+    ep, p2p = mxg.ep.CudaEpOps(), mxg.ep.CudaP2POps()
+    routed = [ep.route(torch.from_numpy(a[0]).to(cuda_dev), E) for a in ins]
+    C = torch.stack([rt[0] for rt in routed])
+    out, _, _ = ep_oracle.simulate([x.float().cpu().numpy() for x in xs], [a[0] for a in ins], E)
+    cap = max(o[0].shape[0] for o in out) + 7
+    bufs = [torch.zeros(cap, H, dtype=torch.bfloat16, device=cuda_dev) for _ in range(world)]
+    ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=cuda_dev)
+    for r in range(world):
+        m_pad = out[r][0].shape[0]
+        pl = p2p.plan(C, r, 32, m_pad, int(out[r][1].sum()))
+        send = torch.full((ns[r] * k, H), 5.0, dtype=torch.bfloat16, device=cuda_dev)
+        p2p.dispatch_gather(xs[r], routed[r][1], pl[0], pl[1], E // world, r, ptrs, cap, ys[r], send)
+        torch.cuda.synchronize()
+        sr = routed[r][1].long()
+        assert torch.equal(send, ys[r][sr])
+    for d in range(world):
+        m_pad = out[d][0].shape[0]
+        assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), out[d][0])
+    assert mxg.device_error() == 0
+
+
 def test_copy_runs_move_rows_and_refuse_out_of_bounds_runs(mxg, cuda_dev):
     """mxg_copy_runs (copy-engine row runs) between buffers of this GPU: the
     dispatch run tables of four emulated ranks put every row where the
