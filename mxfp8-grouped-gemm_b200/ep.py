@@ -558,6 +558,11 @@ class ExpertParallel:
             send = plan.pregathered if plan.pregathered_src is x else None
             if send is None:
                 send = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)
+            else:
+                # allocated on the stream of the dispatch; the copies below may
+                # run on another one: keep the allocator from handing the block
+                # out again before they have read it
+                send.record_stream(torch.cuda.current_stream(send.device))
             plan.pregathered = plan.pregathered_src = None
             self.p2p.copy_runs(send, plan.runs_dispatch, buf.ptrs_host, rows)
             self._barrier(x.device)
