@@ -194,6 +194,17 @@ MXG_API int mxg_grouped_wgrad_run(const void* go, const void* ia, int num_groups
 MXG_API int mxg_quantize_dual(const void* x_bf16, int64_t rows, int64_t cols, void* q_e4m3,
                               void* scales_e8m0, void* qt_e4m3, void* scales_t_e8m0, void* stream);
 
+/* mxg_quantize_dual restricted to rows [row_begin, row_end) of x (both
+ * multiples of 32): the outputs keep the layout of the whole [rows, cols]
+ * tensor and only the bytes of those rows (row-wise) or of those columns of
+ * qt / 32-row blocks of st (column-wise) are written, so encoding a tensor in
+ * row ranges, one launch each, writes the same bytes as one whole-tensor
+ * encode.  Lets the rows of some expert groups be encoded while the rest are
+ * still arriving. */
+MXG_API int mxg_quantize_dual_rows(const void* x_bf16, int64_t rows, int64_t cols, int64_t row_begin,
+                                   int64_t row_end, void* q_e4m3, void* scales_e8m0, void* qt_e4m3,
+                                   void* scales_t_e8m0, void* stream);
+
 /* MXFP8 encodings of h = silu(g) * u for gu rows [g (inter) | u (inter)]
  * (bf16 [rows, 2*inter]) without writing h: bit-identical to mxg_swiglu
  * followed by mxg_quantize_dual on its output.  rows, inter multiples of 32. */
@@ -295,17 +306,24 @@ MXG_API int mxg_ep_dispatch_p2p(const void* src, int64_t src_rows, int64_t row_b
                                 const uint64_t* peer_bufs, int64_t capacity_rows, int max_blocks,
                                 void* stream);
 
-/* mxg_ep_dispatch_p2p of src, and in the same pass row send_rows[p] of src2
- * (same row size and row count as src) copied to row p of gather_out (this
- * GPU's memory, n_send rows): the second tensor put in send order for a
- * later exchange on the copy engines (mxg_copy_runs), while the first one is
- * bound by NVLink.  Default grid. */
+/* mxg_ep_dispatch_p2p of src with two additions, in the same pass (bound by
+ * NVLink, so the local copies ride along):
+ *  - src2 non-null: row send_rows[p] of src2 (same row size and row count as
+ *    src) is copied to row p of gather_out (this GPU's memory, n_send rows):
+ *    a second tensor put in send order for a later exchange on the copy
+ *    engines (mxg_copy_runs);
+ *  - split_h in (0, e_local]: positions of slots whose local expert index
+ *    (slot % e_local) is >= split_h are not stored to their owner; their src
+ *    row goes to row p of src_later (this GPU's memory, n_send rows) instead,
+ *    so that part of the dispatch can follow on the copy engines while the
+ *    owners already work on the experts below split_h.  0: no split.
+ * Default grid. */
 MXG_API int mxg_ep_dispatch_p2p_gather(const void* src, int64_t src_rows, int64_t row_bytes,
                                        const int32_t* send_rows, int64_t n_send,
                                        const int32_t* slot_start, const int32_t* dest_base,
                                        int num_slots, int e_local, int me, const uint64_t* peer_bufs,
                                        int64_t capacity_rows, const void* src2, void* gather_out,
-                                       void* stream);
+                                       int split_h, void* src_later, void* stream);
 
 /* Padded local rows q = ret_order[i] (i < n_rows) -> row back_row[q] of
  * peer_bufs[back_rank[q]] (skipped where back_rank < 0). */

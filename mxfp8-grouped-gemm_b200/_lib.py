@@ -77,7 +77,7 @@ _PROTOS = {
     "mxg_ep_dispatch_p2p": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int,
                                      _c_int, _vp, _c_i64, _c_int, _vp]),
     "mxg_ep_dispatch_p2p_gather": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int,
-                                            _c_int, _vp, _c_i64, _vp, _vp, _vp]),
+                                            _c_int, _vp, _c_i64, _vp, _vp, _c_int, _vp, _vp]),
     "mxg_ep_return_p2p": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_int, _c_i64, _c_int,
                                    _vp]),
     "mxg_ep_zero_pad_rows": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp]),
@@ -86,6 +86,7 @@ _PROTOS = {
     "mxg_set_gemm_sm_limit": (_c_int, [_c_int]),
     "mxg_get_gemm_sm_limit": (_c_int, []),
     "mxg_quantize_dual": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
+    "mxg_quantize_dual_rows": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_swiglu_quantize": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_swiglu_bwd_quantize": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _vp]),
     "mxg_debug_inject_stall": (_c_int, [_c_i64]),

@@ -155,13 +155,17 @@ __device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uin
 // source row outside [0, src_rows) is skipped and reported.  With src2, the
 // same source row of src2 is also copied to row p of gather_out (local): a
 // second tensor put in send order for a later exchange, in the same pass
-// while this one is bound by NVLink.
+// while this one is bound by NVLink.  With split_h > 0, positions of slots
+// whose local expert index (slot % e_local) is >= split_h are not stored to
+// their owner now: their src row goes to row p of src_later (local, send
+// order) for a later exchange on the copy engines.
 __global__ void __launch_bounds__(kCopyThreadsExclusive) p2p_dispatch_kernel(
     const uint4* __restrict__ src, int64_t src_rows, int64_t row_vecs,
     const int32_t* __restrict__ send_rows, int64_t n_send, const int32_t* __restrict__ slot_start,
     const int32_t* __restrict__ dest_base, int E, int e_local, int me,
     const uint64_t* __restrict__ peer_bufs, int64_t capacity_rows, int* err,
-    const uint4* __restrict__ src2, uint4* __restrict__ gather_out) {
+    const uint4* __restrict__ src2, uint4* __restrict__ gather_out, int split_h,
+    uint4* __restrict__ src_later) {
   __shared__ int32_t ss[kMaxSlotsSmem];
   for (int i = threadIdx.x; i <= E; i += blockDim.x) ss[i] = slot_start[i];
   __syncthreads();
@@ -189,8 +193,11 @@ __global__ void __launch_bounds__(kCopyThreadsExclusive) p2p_dispatch_kernel(
       if (lane == 0) atomicCAS(err, 0, MXG_ERR_INVALID_ARGUMENT);
       continue;
     }
-    warp_copy_row(reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs,
-                  src + src_row * row_vecs, row_vecs, lane);
+    if (split_h > 0 && lo % e_local >= split_h)
+      warp_copy_row(src_later + p * row_vecs, src + src_row * row_vecs, row_vecs, lane);
+    else
+      warp_copy_row(reinterpret_cast<uint4*>(peer_bufs[lo / e_local]) + row * row_vecs,
+                    src + src_row * row_vecs, row_vecs, lane);
     if (src2 != nullptr) warp_copy_row(gather_out + p * row_vecs, src2 + src_row * row_vecs, row_vecs, lane);
   }
   __threadfence_system();
@@ -358,7 +365,7 @@ extern "C" int mxg_ep_dispatch_p2p(const void* src, int64_t src_rows, int64_t ro
   if (cl.smem && (st = allow_exclusive_smem(p2p_dispatch_kernel))) return st;
   p2p_dispatch_kernel<<<cl.blocks, cl.threads, cl.smem, (cudaStream_t)stream>>>(
       reinterpret_cast<const uint4*>(src), src_rows, row_bytes / 16, send_rows, n_send, slot_start,
-      dest_base, num_slots, e_local, me, peer_bufs, capacity_rows, err, nullptr, nullptr);
+      dest_base, num_slots, e_local, me, peer_bufs, capacity_rows, err, nullptr, nullptr, 0, nullptr);
   return cuda_status(cudaGetLastError());
 }
 
@@ -367,16 +374,21 @@ extern "C" int mxg_ep_dispatch_p2p_gather(const void* src, int64_t src_rows, int
                                           const int32_t* slot_start, const int32_t* dest_base,
                                           int num_slots, int e_local, int me,
                                           const uint64_t* peer_bufs, int64_t capacity_rows,
-                                          const void* src2, void* gather_out, void* stream) {
+                                          const void* src2, void* gather_out, int split_h,
+                                          void* src_later, void* stream) {
   if (n_send < 0 || src_rows < 0 || row_bytes < 0 || num_slots < 1 || num_slots > MXG_EP_MAX_EXPERTS ||
       e_local < 1 || num_slots % e_local != 0 || capacity_rows < 0 || me < 0 ||
       me >= num_slots / e_local)
     return MXG_ERR_INVALID_ARGUMENT;
   if (row_bytes % 16 != 0) return MXG_ERR_BAD_SHAPE;
   if (n_send == 0 || row_bytes == 0) return MXG_OK;
-  if (!src || !send_rows || !slot_start || !dest_base || !peer_bufs || !src2 || !gather_out)
+  if (!src || !send_rows || !slot_start || !dest_base || !peer_bufs) return MXG_ERR_INVALID_ARGUMENT;
+  if ((src2 == nullptr) != (gather_out == nullptr) || split_h < 0 || split_h > e_local ||
+      (split_h > 0 && !src_later))
     return MXG_ERR_INVALID_ARGUMENT;
-  if (!aligned16(src) || !aligned16(src2) || !aligned16(gather_out)) return MXG_ERR_MISALIGNED;
+  if (!aligned16(src) || (src2 && (!aligned16(src2) || !aligned16(gather_out))) ||
+      (split_h > 0 && !aligned16(src_later)))
+    return MXG_ERR_MISALIGNED;
   int st = check_device();
   if (st) return st;
   int* err = device_error_word();
@@ -385,7 +397,8 @@ extern "C" int mxg_ep_dispatch_p2p_gather(const void* src, int64_t src_rows, int
   p2p_dispatch_kernel<<<cl.blocks, cl.threads, cl.smem, (cudaStream_t)stream>>>(
       reinterpret_cast<const uint4*>(src), src_rows, row_bytes / 16, send_rows, n_send, slot_start,
       dest_base, num_slots, e_local, me, peer_bufs, capacity_rows, err,
-      reinterpret_cast<const uint4*>(src2), reinterpret_cast<uint4*>(gather_out));
+      reinterpret_cast<const uint4*>(src2), reinterpret_cast<uint4*>(gather_out), split_h,
+      reinterpret_cast<uint4*>(src_later));
   return cuda_status(cudaGetLastError());
 }
 

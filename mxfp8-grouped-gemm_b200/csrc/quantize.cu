@@ -178,6 +178,8 @@ struct DualArgs {
   uint8_t* s;        // row-wise scales [rows, cols/32]
   uint8_t* qt;       // column-wise codes [cols, rows] (null: skip)
   uint8_t* st;       // column-wise scales [cols, rows/32]
+  int64_t row0;      // rows [row0, row_end) are encoded (launch_dual sets them;
+  int64_t row_end;   // rows stays the row count the outputs are laid out for)
 };
 
 __device__ __forceinline__ uint4 swiglu_chunk(uint4 g, uint4 u) {
@@ -249,7 +251,7 @@ __device__ __forceinline__ void dual_column_pass(const DualArgs& a, const uint32
 #pragma unroll 1
   for (int it = t; it < kItems; it += NT) {
     const int h = it & 1, pcol = (it >> 1) % CW, rblk = (it >> 1) / CW;
-    const bool row_ok = r0 + 32 * rblk < a.rows;
+    const bool row_ok = r0 + 32 * rblk < a.row_end;
     int64_t col0;
     bool col_ok;
     if (KIND == DUAL_SWIGLU_GRAD) {
@@ -326,7 +328,7 @@ __device__ __forceinline__ void dual_store_col_scales(const DualArgs& a,
       gcol = c0 + t;
       if (gcol >= a.cols) return;
     }
-    const int64_t rem = (a.rows - r0) / 32;
+    const int64_t rem = (a.row_end - r0) / 32;
     const int nb = int(rem < R / 32 ? rem : R / 32);
     uint8_t* dst = a.st + gcol * (a.rows / 32) + r0 / 32;
     if (R / 32 == 4 && nb == 4 && (reinterpret_cast<uintptr_t>(dst) & 3u) == 0) {
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
   constexpr int CPR = kTileCols / 8;                     // 16-byte chunks per tile row
   __shared__ __align__(16) uint32_t tile[R][CW];
   __shared__ __align__(4) uint8_t col_scales[kTileCols][R / 32];  // column pass -> one write per column
-  const int64_t r0 = int64_t(blockIdx.y) * R;
+  const int64_t r0 = a.row0 + int64_t(blockIdx.y) * R;
   const int t = threadIdx.x;
   // tile columns -> tensor columns: contiguous, except for the gradient where
   // the first half of the tile is dg[j0 + c] and the second du[j0 + c]
@@ -357,7 +359,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
       const int r = k / CPR, ch = k % CPR;
       const int64_t col = c0 + ch * 8;
       v[i] = make_uint4(0, 0, 0, 0);
-      if (col < a.cols && r0 + r < a.rows) {
+      if (col < a.cols && r0 + r < a.row_end) {
         if (KIND == DUAL_PLAIN) {
           v[i] = __ldcs(a.a + ((r0 + r) * a.cols + col) / 8);
         } else {
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
       const int k = t + 256 * i;
       const int r = k / CPR, ch = k % CPR;
       const int64_t col = c0 + ch * 8;
-      const bool valid = col < a.cols && r0 + r < a.rows;
+      const bool valid = col < a.cols && r0 + r < a.row_end;
       if (a.q) encode_row_chunk(a, v[i], r0 + r, col, valid);
       *reinterpret_cast<uint4*>(&tile[r][(ch ^ (((r >> 4) & 1) << 2)) * 4]) = v[i];
     }
@@ -385,7 +387,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
       const int64_t j = c0 + ch * 8;
       dg[i] = make_uint4(0, 0, 0, 0);
       du[i] = dg[i];
-      if (j < a.inter && r0 + r < a.rows) {
+      if (j < a.inter && r0 + r < a.row_end) {
         const uint4* rowp = a.a + (r0 + r) * (2 * a.inter) / 8;
         const uint4 g = __ldcs(rowp + j / 8), u = __ldcs(rowp + (a.inter + j) / 8);
         const uint4 d = __ldcs(a.dh + ((r0 + r) * a.inter + j) / 8);
@@ -400,7 +402,7 @@ __global__ void __launch_bounds__(256, 3) quant_dual_kernel(DualArgs a) {
       const int k = t + 256 * i;
       const int r = k / JCPR, ch = k % JCPR;
       const int64_t j = c0 + ch * 8;
-      const bool valid = j < a.inter && r0 + r < a.rows;
+      const bool valid = j < a.inter && r0 + r < a.row_end;
       if (a.q) {
         encode_row_chunk(a, dg[i], r0 + r, j, valid);
         encode_row_chunk(a, du[i], r0 + r, a.inter + j, valid);
@@ -580,7 +582,7 @@ static bool launch_dual_tma(const DualArgs& a, void* stream, int* status) {
   if constexpr (KIND == DUAL_SWIGLU) {
     return false;
   } else {
-    if (a.q != nullptr) return false;
+    if (a.q != nullptr || a.row0 != 0 || a.row_end != a.rows) return false;
     if (KIND == DUAL_SWIGLU_GRAD && (a.inter % 32 != 0 || !aligned16(a.dh))) return false;
     const int per_sm = quant_tma_blocks_per_sm<KIND>();
     const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
@@ -600,15 +602,23 @@ static bool launch_dual_tma(const DualArgs& a, void* stream, int* status) {
   }
 }
 
+// Encodes rows [row0, row_end) of the tensor (row_end < 0: all rows); the
+// outputs keep the layout of the whole tensor, so a split encode (rows of some
+// groups now, the rest later) writes the same bytes as one over all rows.
 template <int KIND>
-static int launch_dual(DualArgs a, void* stream) {
+static int launch_dual(DualArgs a, void* stream, int64_t row0 = 0, int64_t row_end = -1) {
   if (a.rows < 0 || a.cols < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if (row_end < 0) row_end = a.rows;
+  if (row0 < 0 || row0 > row_end || row_end > a.rows) return MXG_ERR_INVALID_ARGUMENT;
+  if (row0 % 32 != 0 || row_end % 32 != 0) return MXG_ERR_BAD_SHAPE;
+  a.row0 = row0;
+  a.row_end = row_end;
   if ((a.q == nullptr) != (a.s == nullptr) || (a.qt == nullptr) != (a.st == nullptr) ||
       (a.q == nullptr && a.qt == nullptr))
     return MXG_ERR_INVALID_ARGUMENT;
   if (a.rows % 32 != 0 || a.cols % 32 != 0) return MXG_ERR_BAD_SHAPE;
   if ((a.q && !aligned16(a.q)) || (a.qt && !aligned16(a.qt))) return MXG_ERR_MISALIGNED;
-  if (a.rows == 0 || a.cols == 0) return MXG_OK;
+  if (row_end == row0 || a.cols == 0) return MXG_OK;
   if ((a.rows + kTileRows - 1) / kTileRows > 65535) return MXG_ERR_BAD_SHAPE;
   int e = check_device();
   if (e) return e;
@@ -616,7 +626,7 @@ static int launch_dual(DualArgs a, void* stream) {
   if (launch_dual_tma<KIND>(a, stream, &tma_status)) return tma_status;
   const int64_t span = KIND == DUAL_SWIGLU_GRAD ? a.inter : a.cols;
   const int64_t per = KIND == DUAL_SWIGLU_GRAD ? kTileCols / 2 : kTileCols;
-  dim3 grid(unsigned((span + per - 1) / per), unsigned((a.rows + kTileRows - 1) / kTileRows));
+  dim3 grid(unsigned((span + per - 1) / per), unsigned((row_end - row0 + kTileRows - 1) / kTileRows));
   quant_dual_kernel<KIND><<<grid, 256, 0, (cudaStream_t)stream>>>(a);
   return cuda_status(cudaGetLastError());
 }
@@ -707,6 +717,17 @@ extern "C" int mxg_quantize_dual(const void* x_bf16, int64_t rows, int64_t cols,
              reinterpret_cast<uint8_t*>(q_e4m3), reinterpret_cast<uint8_t*>(scales_e8m0),
              reinterpret_cast<uint8_t*>(qt_e4m3), reinterpret_cast<uint8_t*>(scales_t_e8m0)};
   return launch_dual<DUAL_PLAIN>(a, stream);
+}
+
+extern "C" int mxg_quantize_dual_rows(const void* x_bf16, int64_t rows, int64_t cols, int64_t row_begin,
+                                      int64_t row_end, void* q_e4m3, void* scales_e8m0, void* qt_e4m3,
+                                      void* scales_t_e8m0, void* stream) {
+  if (!x_bf16 || row_end < 0) return MXG_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x_bf16)) return MXG_ERR_MISALIGNED;
+  DualArgs a{reinterpret_cast<const uint4*>(x_bf16), nullptr, rows, cols, 0,
+             reinterpret_cast<uint8_t*>(q_e4m3), reinterpret_cast<uint8_t*>(scales_e8m0),
+             reinterpret_cast<uint8_t*>(qt_e4m3), reinterpret_cast<uint8_t*>(scales_t_e8m0)};
+  return launch_dual<DUAL_PLAIN>(a, stream, row_begin, row_end);
 }
 
 extern "C" int mxg_swiglu_quantize(const void* gu_bf16, int64_t rows, int64_t inter, void* q_e4m3,

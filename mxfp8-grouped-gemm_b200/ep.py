@@ -126,17 +126,20 @@ class CudaP2POps:
                                               _lib.stream_ptr(src.device)), "mxg_ep_dispatch_p2p")
 
     def dispatch_gather(self, src, send_rows, slot_start, dest_base, e_local, me, peer_ptrs, capacity_rows,
-                        src2, gather_out):
-        """dispatch of src, and src2's rows put in send order into gather_out
-        in the same pass."""
-        src, src2 = src.contiguous(), src2.contiguous()
+                        src2=None, gather_out=None, split_h=0, src_later=None):
+        """dispatch of src, with src2's rows put in send order into gather_out
+        in the same pass, and (split_h > 0) the rows of local experts >=
+        split_h put in send order into src_later instead of being sent."""
+        src = src.contiguous()
         row_bytes = src.element_size() * (src[0].numel() if src.shape[0] else 0)
+        if src.numel() == 0:
+            return
+        ptr = lambda t: None if t is None else t.data_ptr()
         _lib.check(self.L.mxg_ep_dispatch_p2p_gather(
-            src.data_ptr() if src.numel() else None, src.shape[0], row_bytes, send_rows.data_ptr(),
-            send_rows.numel(), slot_start.data_ptr(), dest_base.data_ptr(), dest_base.numel(), e_local, me,
-            peer_ptrs.data_ptr(), capacity_rows, src2.data_ptr() if src2.numel() else None,
-            gather_out.data_ptr() if gather_out.numel() else None, _lib.stream_ptr(src.device)),
-            "mxg_ep_dispatch_p2p_gather")
+            src.data_ptr(), src.shape[0], row_bytes, send_rows.data_ptr(), send_rows.numel(),
+            slot_start.data_ptr(), dest_base.data_ptr(), dest_base.numel(), e_local, me, peer_ptrs.data_ptr(),
+            capacity_rows, ptr(None if src2 is None else src2.contiguous()), ptr(gather_out), split_h,
+            ptr(src_later), _lib.stream_ptr(src.device)), "mxg_ep_dispatch_p2p_gather")
 
     def ret(self, src, ret_order, back_rank, back_row, peer_ptrs, capacity_rows, max_blocks=0):
         src = src.contiguous()
@@ -279,7 +282,7 @@ def balanced_placement(expert_load, world: int, refine_iters: int = 2000) -> np.
     return slot
 
 
-def copy_run_tables(counts_all: np.ndarray, me: int, pad: int):
+def copy_run_tables(counts_all: np.ndarray, me: int, pad: int, first_slot: int = 0):
     """Copy-engine runs of rank ``me`` from the gathered slot counts C
     [world, E] (the layout of ``mxg_ep_p2p_plan``: slot s of rank s // E_local
     holds the rows of every source rank in rank order, groups padded to
@@ -289,41 +292,32 @@ def copy_run_tables(counts_all: np.ndarray, me: int, pad: int):
     peers at the same time):
       dispatch: send positions [pref[me][s], pref[me][s+1]) of slot s (rows of
                 the send-order buffer) -> rows [dest_base[s] + pref[me][s], ..)
-                of rank s // E_local;
+                of rank s // E_local (only slots with s % E_local >= first_slot);
       return:   padded rows [gs[s] + sum_{r'<r} C[r'][s], .. + C[r][s]) of local
                 slot s -> rows [pref[r][s], ..) of rank r's return buffer."""
     C = np.asarray(counts_all, dtype=np.int64)
     W, E = C.shape
     El = E // W
     pref = np.concatenate([np.zeros((W, 1), np.int64), np.cumsum(C, axis=1)], axis=1)
-    padded = (C.sum(0) + pad - 1) // pad * pad
-    gs = np.zeros(E, np.int64)
-    for d in range(W):
-        gs[d * El:(d + 1) * El] = np.concatenate([[0], np.cumsum(padded[d * El:(d + 1) * El])[:-1]])
-    before = np.concatenate([np.zeros((1, E), np.int64), np.cumsum(C, axis=0)[:-1]], axis=0)  # rows of ranks < r
-    order = [(me + i) % W for i in range(1, W + 1)]
-    d_rows, d_src, d_dst, d_rank = [], [], [], []
-    for d in order:
-        for s in range(d * El, (d + 1) * El):
-            c = C[me, s]
-            if c:
-                d_src.append(pref[me, s])
-                d_dst.append(gs[s] + before[me, s])
-                d_rows.append(c)
-                d_rank.append(d)
-    r_rows, r_src, r_dst, r_rank = [], [], [], []
-    for r in order:
-        for s in range(me * El, (me + 1) * El):
-            c = C[r, s]
-            if c:
-                r_src.append(gs[s] + before[r, s])
-                r_dst.append(pref[r, s])
-                r_rows.append(c)
-                r_rank.append(r)
+    padded = ((C.sum(0) + pad - 1) // pad * pad).reshape(W, El)
+    gs = (np.cumsum(padded, axis=1) - padded).reshape(E)         # padded start of each slot on its owner
+    before = np.cumsum(C, axis=0) - C                             # rows of ranks < r in each slot
+    order = (me + 1 + np.arange(W)) % W
+    slots = (order[:, None] * El + np.arange(first_slot, El)).reshape(-1)  # owners' slots, owner me+1 first
+    c = C[me, slots]
+    keep = c > 0
+    ds = slots[keep]
+    dispatch = (pref[me, ds], gs[ds] + before[me, ds], c[keep], ds // El)
+    rr = np.repeat(order, El)                                     # source ranks, me+1 first
+    ss = np.tile(me * El + np.arange(El), W)                      # my slots
+    c = C[rr, ss]
+    keep = c > 0
+    rr, ss = rr[keep], ss[keep]
+    ret = (gs[ss] + before[rr, ss], pref[rr, ss], c[keep], rr)
     i64 = lambda v: np.ascontiguousarray(v, dtype=np.int64)
     i32 = lambda v: np.ascontiguousarray(v, dtype=np.int32)
-    return ((i64(d_src), i64(d_dst), i64(d_rows), i32(d_rank)),
-            (i64(r_src), i64(r_dst), i64(r_rows), i32(r_rank)))
+    return ((i64(dispatch[0]), i64(dispatch[1]), i64(dispatch[2]), i32(dispatch[3])),
+            (i64(ret[0]), i64(ret[1]), i64(ret[2]), i32(ret[3])))
 
 
 @dataclass
@@ -351,6 +345,10 @@ class DispatchPlan:
     runs_return: tuple | None = None         # padded rows of each (local expert, source rank) -> home
     pregathered: torch.Tensor | None = None  # [n*k, H'] a second tensor already in send order
     pregathered_src: torch.Tensor | None = None  # ... namely this one
+    # split dispatch: local expert slots >= split of every owner still to come
+    split: int = 0
+    later: torch.Tensor | None = None        # [n*k, H] their rows in send order
+    runs_later: tuple | None = None          # their copy-engine runs
 
 
 class ExpertParallel:
@@ -390,6 +388,11 @@ class ExpertParallel:
         self.buffers = {}        # name -> PeerBuffer
         self.capacity = {}       # name -> rows
         self._flag = None
+        self.marker = None       # optional callable(name): a timing mark on the current stream
+
+    def _mark(self, name):
+        if self.marker is not None:
+            self.marker(name)
 
     def close(self):
         """Release the peer buffers (collective: every rank calls it).  Every
@@ -448,13 +451,19 @@ class ExpertParallel:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
         return out
 
-    def dispatch(self, x: torch.Tensor, expert_ids: torch.Tensor, also_gather: torch.Tensor | None = None):
+    def dispatch(self, x: torch.Tensor, expert_ids: torch.Tensor, also_gather: torch.Tensor | None = None,
+                 split: int = 0):
         """x [n, H] token rows, expert_ids [n, k] global expert of each choice.
         Returns (x_local [M_pad, H] expert-major 32-padded rows of this rank's
-        expert slots, plan).  also_gather ([n, H] like x, peer-memory
-        transport): put its rows in send order in the same pass
-        (``plan.pregathered``), for a later ``dispatch_like(...,
-        copy_engines=True)`` of that tensor."""
+        expert slots, plan).  Peer-memory transport only:
+          also_gather ([n, H] like x): put its rows in send order in the same
+          pass (``plan.pregathered``), for a later ``dispatch_like(...,
+          copy_engines=True)`` of that tensor;
+          split in (0, E_local): only the rows of every owner's local slots
+          below ``split`` arrive now; the rest wait in send order for
+          ``dispatch_rest(plan)`` (copy engines), so the owners can start on
+          their first ``split`` experts meanwhile (``plan.split`` says whether
+          the split was taken)."""
         n, k = expert_ids.shape
         slot_map = None
         if self.placement is not None:
@@ -463,7 +472,7 @@ class ExpertParallel:
             slot_map = self.slot_of_expert
         counts, send_rows, slot_pos = self.ops.route(expert_ids, self.num_experts, slot_map)
         if self.transport == "p2p":
-            return self._dispatch_p2p(x, n, k, counts, send_rows, slot_pos, also_gather)
+            return self._dispatch_p2p(x, n, k, counts, send_rows, slot_pos, also_gather, split)
         recv_counts = self._a2a(counts, counts.numel()).view(self.world, self.e_local)
         host = torch.cat([counts, recv_counts.reshape(-1)]).cpu().view(2, self.world, self.e_local)
         sc = host[0].sum(1).tolist()
@@ -478,7 +487,7 @@ class ExpertParallel:
                             n_recv, n, k)
         return self.dispatch_like(x, plan), plan
 
-    def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos, also_gather=None):
+    def _dispatch_p2p(self, x, n, k, counts, send_rows, slot_pos, also_gather=None, split=0):
         E, W, El, pad = self.num_experts, self.world, self.e_local, self.pad
         # every rank's slot counts plus its number of routing slots n*k: a
         # routing slot whose expert id is out of range is counted nowhere, and
@@ -487,6 +496,7 @@ class ExpertParallel:
         mine = torch.cat([counts, torch.full((1,), n * k, dtype=torch.int32, device=x.device)])
         Cx = torch.empty(W * (E + 1), dtype=torch.int32, device=x.device)
         dist.all_gather_into_tensor(Cx, mine, group=self.group)   # also: every receiver is idle
+        self._mark("x.counts")
         Cx = Cx.view(W, E + 1)
         Chx = Cx.cpu().numpy().astype(np.int64)
         Ch = Chx[:, :E]
@@ -517,26 +527,51 @@ class ExpertParallel:
             self._ensure_ret(name, x.device)
         slot_start, dest_base, group_rows, _, back_rank, back_row, ret_order = self.p2p.plan(
             C, self.rank, pad, m_pad, recv_rows)
-        send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
-        recv_splits = Ch[:, self.rank * El:(self.rank + 1) * El].sum(1).tolist()
-        runs_d, runs_r = copy_run_tables(Ch, self.rank, pad)
-        plan = DispatchPlan(send_rows, slot_pos, send_splits, recv_splits, None, None,
+        plan = DispatchPlan(send_rows, slot_pos, None, None, None, None,
                             group_rows, padded[self.rank].tolist(), recv_rows, n, k,
-                            slot_start, dest_base, back_rank, back_row, ret_order, runs_d, runs_r)
-        if also_gather is not None and tuple(also_gather.shape) == tuple(x.shape) \
-                and also_gather.dtype == x.dtype:
-            m_pad = plan.back_rank.numel()
+                            slot_start, dest_base, back_rank, back_row, ret_order)
+        split = int(split) if 0 < int(split) < El else 0
+        like = also_gather is not None and tuple(also_gather.shape) == tuple(x.shape) \
+            and also_gather.dtype == x.dtype
+        if like or split:
             buf = self.buffers["x"]
             rows, _ = self.capacity["x"]
             local = buf.view(m_pad, x)
             self.p2p.zero_pad_rows(local, plan.back_rank)
-            send = torch.empty((n * k,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+            self._mark("x.plan")
+            send = torch.empty((n * k,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device) if like else None
+            later = torch.empty((n * k,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device) if split else None
             self.p2p.dispatch_gather(x, send_rows, slot_start, dest_base, El, self.rank, buf.ptrs, rows,
-                                     also_gather, send)
+                                     also_gather if like else None, send, split, later)
+            self._mark("x.send")
             self._barrier(x.device)
-            plan.pregathered, plan.pregathered_src = send, also_gather
-            return local, plan
-        return self.dispatch_like(x, plan, "x"), plan
+            plan.pregathered, plan.pregathered_src = (send, also_gather) if like else (None, None)
+            plan.split, plan.later = split, later
+        else:
+            local = self.dispatch_like(x, plan, "x")
+        # host tables built while the rows move
+        plan.send_splits = Ch[self.rank].reshape(W, El).sum(1).tolist()
+        plan.recv_splits = Ch[:, self.rank * El:(self.rank + 1) * El].sum(1).tolist()
+        plan.runs_dispatch, plan.runs_return = copy_run_tables(Ch, self.rank, pad)
+        if split:
+            plan.runs_later = copy_run_tables(Ch, self.rank, pad, first_slot=split)[0]
+        return local, plan
+
+    def dispatch_rest(self, plan: DispatchPlan) -> None:
+        """Second half of a split ``dispatch``: the rows of every owner's local
+        slots >= plan.split, from their send-order copy, by copy-engine runs
+        into the owners' "x" receive buffers (the tensor ``dispatch``
+        returned); returns on the current stream once every rank's rows have
+        landed.  Collective: every rank calls it after the same dispatch."""
+        if not plan.split or plan.later is None:
+            raise ValueError("dispatch_rest follows a dispatch(..., split=h) that took the split")
+        send = plan.later
+        # allocated on the dispatch's stream; the copies may run on another
+        send.record_stream(torch.cuda.current_stream(send.device))
+        plan.later = None
+        rows, _ = self.capacity["x"]
+        self.p2p.copy_runs(send, plan.runs_later, self.buffers["x"].ptrs_host, rows)
+        self._barrier(send.device)
 
     def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy",
                       copy_engines: bool = False) -> torch.Tensor:
@@ -578,8 +613,12 @@ class ExpertParallel:
                 raise ValueError("row size differs from the receive buffer's")
             local = buf.view(m_pad, x)
             self.p2p.zero_pad_rows(local, plan.back_rank)
+            if buffer == "x":
+                self._mark("x.plan")
             self.p2p.dispatch(x, plan.send_rows, plan.slot_start, plan.dest_base, self.e_local,
                               self.rank, buf.ptrs, rows, self.p2p_max_blocks)
+            if buffer == "x":
+                self._mark("x.send")
             self._barrier(x.device)
             return local
         send_buf = self.ops.gather(x, plan.send_rows, plan.n_tokens * plan.topk)

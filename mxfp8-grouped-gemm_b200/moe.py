@@ -51,7 +51,7 @@ class ExpertFFN:
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
                  wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True,
-                 copy_engines: bool = False, fused_return: bool = False):
+                 copy_engines: bool = False, fused_return: bool = False, split_experts: int = 0):
         """With a comm stream, the dy dispatch and the returns run beside the
         GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
         they do, and runs the peer copies only there.  wgrad_dtype is the
@@ -66,7 +66,12 @@ class ExpertFFN:
         dgrad store their result rows straight into the tokens' home ranks
         from their epilogues (no local result tensor, no separate return;
         measured slower than a separate return on 2 B200s: the epilogue's
-        64-byte peer stores hold the GEMM back)."""
+        64-byte peer stores hold the GEMM back).  split_experts (with copy
+        engines and the peer-memory transport): the x dispatch sends the rows
+        of every rank's first split_experts local experts with the SM kernel
+        and the rest by copy-engine runs on the comm stream, while this rank
+        encodes and multiplies its first split_experts groups; 0: one
+        dispatch."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
@@ -94,6 +99,7 @@ class ExpertFFN:
         self.comm = comm_stream
         self.ce = bool(copy_engines and comm_stream is not None)
         self.fused_return = bool(fused_return and ep.transport == "p2p")
+        self.split = int(split_experts) if (self.ce and ep.transport == "p2p" and 0 < split_experts < E) else 0
         self.reserve = reserve_sms if comm_stream is not None else 0
         if self.reserve:
             self.ep.p2p_max_blocks = self.reserve
@@ -114,6 +120,14 @@ class ExpertFFN:
         q, s = a
         wq, ws = w
         return ops.grouped_fwd(q, wq, offs, s, ws, out_dtype=out_dtype, offs_kind=_lib.OFFS_SIZES)
+
+    def _fwd_groups(self, a, w, offs, g0, g1, r0, r1, out):
+        """Grouped forward of groups [g0, g1), whose padded rows are [r0, r1),
+        into rows [r0, r1) of out."""
+        q, s = a
+        wq, ws = w
+        ops.grouped_fwd(q[r0:r1], wq[g0:g1], offs[g0:g1], s[r0:r1], ws[g0:g1], out=out[r0:r1],
+                        offs_kind=_lib.OFFS_SIZES)
 
     def _fwd_home(self, a, w, offs, like, buffer):
         """Grouped forward whose result rows go straight to their home ranks'
@@ -143,24 +157,50 @@ class ExpertFFN:
         comm = self.comm
         side = (lambda: torch.cuda.stream(comm)) if comm is not None else nullcontext
         self._mark("start")
+        ep.marker = self._mark if self.marks is not None else None
         # with copy-engine exchanges, dy is put in send order during the x
         # dispatch (that pass is bound by NVLink), not by a gather beside the GEMMs
-        x_local, plan = ep.dispatch(x, expert_ids, also_gather=dy if self.ce else None)
+        x_local, plan = ep.dispatch(x, expert_ids, also_gather=dy if self.ce else None, split=self.split)
+        ep.marker = None
         self._plan = plan
         offs = plan.group_rows
         self._mark("dispatch_x")
         if comm is not None:
             comm.wait_stream(main)
         with side():
+            if plan.split:
+                ep.dispatch_rest(plan)                      # the other experts' rows, copy engines
+                x_rest = torch.cuda.Event()
+                x_rest.record()
             dy_local = ep.dispatch_like(dy, plan, copy_engines=self.ce)
             dy_ready = torch.cuda.Event()
             dy_ready.record()
         if comm is None:
             self._mark("dispatch_dy")
-        xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
-        self._mark("quantize_x")
-        with ops.gemm_sm_limit(self.gemm_sms):             # beside the dy exchange
-            gu = self._fwd((xq, xs), self.wgu, offs)
+        if plan.split:
+            # groups [0, h) while the rest arrive; the encodes write the
+            # bytes one whole-tensor encode would
+            h, M = plan.split, x_local.shape[0]
+            ra = int(sum(plan.group_rows_host[:h]))
+            xo = ops.dual_outputs(x_local)
+            xq, xs, ia_g, ias_g = xo
+            gu = torch.empty(M, 2 * self.I, dtype=torch.bfloat16, device=x_local.device)
+            ops.quantize_dual_rows(x_local, 0, ra, xo)
+            self._mark("quantize_x")
+            with ops.gemm_sm_limit(self.gemm_sms):
+                self._fwd_groups((xq, xs), self.wgu, offs, 0, h, 0, ra, gu)
+            self._mark("fwd_gate_up")
+            main.wait_event(x_rest)
+            self._mark("wait_x_rest")
+            ops.quantize_dual_rows(x_local, ra, M, xo)
+            self._mark("quantize_x")
+            with ops.gemm_sm_limit(self.gemm_sms):
+                self._fwd_groups((xq, xs), self.wgu, offs, h, self.E, ra, M, gu)
+        else:
+            xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
+            self._mark("quantize_x")
+            with ops.gemm_sm_limit(self.gemm_sms):             # beside the dy exchange
+                gu = self._fwd((xq, xs), self.wgu, offs)
         self._mark("fwd_gate_up")
         hq, hs, ia_d, ias_d = ops.swiglu_quantize(gu)        # h is never written in bf16
         self._mark("swiglu_quantize_h")

@@ -110,6 +110,31 @@ def quantize_dual(x: torch.Tensor, *, rowwise=True, colwise=True):
     return q, s, qt, st
 
 
+def quantize_dual_rows(x: torch.Tensor, row_begin: int, row_end: int, out):
+    """``quantize_dual`` of rows [row_begin, row_end) of x [R, C] (multiples
+    of 32) into out = (q, s, qt, st) laid out for all R rows (``quantize_dual``
+    shapes; None entries skip that direction): encoding x range by range
+    writes the same bytes as one ``quantize_dual(x)``."""
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("x must be a 2-D bf16 tensor")
+    x = x.contiguous()
+    R, C = x.shape
+    q, s, qt, st = out
+    for t, shape, name in ((q, (R, C), "q"), (s, (R, C // 32), "s"), (qt, (C, R), "qt"), (st, (C, R // 32), "st")):
+        if t is not None and (tuple(t.shape) != shape or not t.is_contiguous() or t.device != x.device):
+            raise ValueError(f"{name} must be a contiguous {shape} tensor on {x.device}")
+    _lib.check(_lib.load().mxg_quantize_dual_rows(x.data_ptr(), R, C, int(row_begin), int(row_end), _lib.ptr(q),
+                                                  _lib.ptr(s), _lib.ptr(qt), _lib.ptr(st),
+                                                  _lib.stream_ptr(x.device)), "mxg_quantize_dual_rows")
+    return out
+
+
+def dual_outputs(x: torch.Tensor, *, rowwise=True, colwise=True):
+    """Empty (q, s, qt, st) for ``quantize_dual_rows`` of x [R, C]."""
+    return _dual_outputs(x.shape[0], x.shape[1], x.device, rowwise, colwise)
+
+
 def swiglu_quantize(gu: torch.Tensor, *, rowwise=True, colwise=True):
     """MXFP8 encodings of h = silu(g) * u for gu = [g | u] ([R, 2I] bf16)
     without materialising h; same bytes as ``quantize_dual(swiglu(gu))``."""

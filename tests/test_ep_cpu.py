@@ -250,3 +250,41 @@ def test_copy_run_tables_place_rows_like_the_oracle(world):
                 if q == r:
                     back[b:b + c] = out[d][0][a:a + c]
         assert np.array_equal(back, xs[r][routed[r][1]])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_dispatch_runs_cover_the_later_slots_once(world):
+    """A split dispatch: the rows of local slots below h (the SM kernel's
+    share) plus the copy-engine runs of ``copy_run_tables(.., first_slot=h)``
+    fill every owner's receive layout exactly as one whole dispatch does, and
+    no later run writes a row of a slot below h."""
+    from conftest import load_pkg
+    ep = load_pkg().ep
+    E, k, H = 4 * world, 3, 8
+    El = E // world
+    xs, ids = [], []
+    for r in range(world):
+        i, x, _ = make_rank_inputs(r, [40, 0, 77, 5][r], k, E, H, zipf=1.1)
+        xs.append(x), ids.append(i)
+    out, routed, _ = ep_oracle.simulate(xs, ids, E)
+    C = np.stack([rt[0] for rt in routed])
+    pref = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(C, axis=1)], axis=1)
+    for h in range(1, El):
+        bufs = [np.zeros_like(o[0]) for o in out]
+        for r in range(world):
+            send = xs[r][routed[r][1]]
+            for s in range(E):                        # the SM kernel's share: slots below h
+                if s % El < h:
+                    (src, dst, rows, rank), _ = ep.copy_run_tables(C, r, 32)
+                    for a, b, c, d in zip(src, dst, rows, rank):
+                        if pref[r, s] <= a < pref[r, s + 1]:
+                            bufs[d][b:b + c] = send[a:a + c]
+            (src, dst, rows, rank), _ = ep.copy_run_tables(C, r, 32, first_slot=h)
+            slot_of_pos = np.searchsorted(pref[r], src, side="right") - 1
+            assert np.all(slot_of_pos % El >= h)
+            assert rows.sum() == sum(C[r, s] for s in range(E) if s % El >= h)
+            for a, b, c, d in zip(src, dst, rows, rank):
+                assert not bufs[d][b:b + c].any()     # each row written once
+                bufs[d][b:b + c] = send[a:a + c]
+        for d in range(world):
+            assert np.array_equal(bufs[d], out[d][0])

@@ -251,11 +251,16 @@ def test_p2p_dispatch_skips_unrouted_positions_and_bad_source_rows(mxg, cuda_dev
     assert torch.all(buf[m_pad:] == 0)
 
 
-def test_p2p_dispatch_gather_moves_rows_and_orders_the_second_tensor(mxg, cuda_dev):
+@pytest.mark.parametrize("split", [0, 2])
+def test_p2p_dispatch_gather_moves_rows_and_orders_the_second_tensor(mxg, cuda_dev, split):
     """mxg_ep_dispatch_p2p_gather with four ranks emulated on one GPU: the
     first tensor lands exactly as mxg_ep_dispatch_p2p puts it (the oracle's
-    layout), the second comes out in send order (src2[send_rows])."""
+    layout), the second comes out in send order (src2[send_rows]).  Split at
+    local slot 2: the owners receive only the rows of their slots 0 and 1,
+    and the rows of slots 2 and 3 come out in send order in the later
+    buffer."""
     world, E, k, H = 4, 16, 3, 64
+    El = E // world
     ns = [300, 0, 517, 64]
     ins = [make_rank_inputs(r, ns[r], k, E, H, zipf=1.1) for r in range(world)]
     xs = [_bf16(a[1], cuda_dev) for a in ins]
@@ -267,17 +272,29 @@ def test_p2p_dispatch_gather_moves_rows_and_orders_the_second_tensor(mxg, cuda_d
     cap = max(o[0].shape[0] for o in out) + 7
     bufs = [torch.zeros(cap, H, dtype=torch.bfloat16, device=cuda_dev) for _ in range(world)]
     ptrs = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=cuda_dev)
+    Ch = C.cpu().numpy().astype(np.int64)
     for r in range(world):
         m_pad = out[r][0].shape[0]
         pl = p2p.plan(C, r, 32, m_pad, int(out[r][1].sum()))
         send = torch.full((ns[r] * k, H), 5.0, dtype=torch.bfloat16, device=cuda_dev)
-        p2p.dispatch_gather(xs[r], routed[r][1], pl[0], pl[1], E // world, r, ptrs, cap, ys[r], send)
+        later = torch.full((ns[r] * k, H), 7.0, dtype=torch.bfloat16, device=cuda_dev) if split else None
+        p2p.dispatch_gather(xs[r], routed[r][1], pl[0], pl[1], El, r, ptrs, cap, ys[r], send, split, later)
         torch.cuda.synchronize()
         sr = routed[r][1].long()
         assert torch.equal(send, ys[r][sr])
+        if split:
+            pos_slot = np.repeat(np.arange(E), Ch[r])          # slot of each send position
+            late = torch.from_numpy(pos_slot % El >= split).to(cuda_dev)
+            assert torch.equal(later[late], xs[r][sr][late])
+            assert bool((later[~late] == 7.0).all())
+    tot = Ch.sum(0).reshape(world, El)
+    padded = (tot + 31) // 32 * 32
     for d in range(world):
         m_pad = out[d][0].shape[0]
-        assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), out[d][0])
+        want = out[d][0].copy()
+        if split:
+            want[padded[d, :split].sum():] = 0                   # slots >= split: not sent yet
+        assert np.array_equal(bufs[d][:m_pad].float().cpu().numpy(), want)
     assert mxg.device_error() == 0
 
 
@@ -473,3 +490,99 @@ def test_expert_ffn_world1(mxg, cuda_dev, wgrad_dtype):
     for name, g, rq, rf in zip(("out", "dx", "dw_gate_up", "dw_down"), got, ref[True], ref[False]):
         eq, ef = orc_mod.rel_frobenius(g, rq), orc_mod.rel_frobenius(g, rf)
         assert eq <= 3e-2 and ef <= 0.12, (name, eq, ef)
+
+
+_LAYER_MODES = {  # name -> (comm stream, copy engines, fused returns, split experts)
+    "seq": (False, False, False, 0), "sm": (True, False, False, 0), "ce": (True, True, False, 0),
+    "ce_split": (True, True, False, 2), "fused": (True, False, True, 0)}
+
+
+def _layer_problem(E, H, I, ns, k):
+    rng = np.random.default_rng(11)
+    f = lambda a: a.astype(np.float32)
+    wgu, wd = f(rng.standard_normal((E, 2 * I, H)) * 0.05), f(rng.standard_normal((E, H, I)) * 0.05)
+    toks = []
+    for n in ns:
+        x, dy = f(rng.standard_normal((n, H))), f(rng.standard_normal((n, H)) * 1e-2)
+        ids = np.stack([rng.choice(E, k, replace=False) for _ in range(n)]).astype(np.int32)
+        p = rng.random((n, k)) + 0.1
+        toks.append((x, dy, ids, f(p / p.sum(1, keepdims=True))))
+    return wgu, wd, toks
+
+
+def _layer_worker(rank, world, port, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        from conftest import load_pkg
+        mxg = load_pkg()
+        dev = torch.device("cuda", rank)
+        E, H, I, k = 8, 256, 128, 2
+        El = E // world
+        wgu, wd, toks = _layer_problem(E, H, I, [300, 217], k)
+        x, dy, ids, p = toks[rank]
+        bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)
+        res = {}
+        for name, (side, ce, fused, split) in _LAYER_MODES.items():
+            par = mxg.ExpertParallel(E, transport="p2p")
+            layer = mxg.moe.ExpertFFN(par, bf(wgu[rank * El:(rank + 1) * El]), bf(wd[rank * El:(rank + 1) * El]),
+                                      comm_stream=torch.cuda.Stream() if side else None, copy_engines=ce,
+                                      fused_return=fused, split_experts=split)
+            for _ in range(2):     # the second step reuses the receive buffers
+                r = layer.step(bf(x), torch.from_numpy(ids).to(dev), torch.from_numpy(p).to(dev), bf(dy))
+            torch.cuda.synchronize()
+            assert mxg.device_error() == 0
+            res[name] = tuple(t.float().cpu().numpy() for t in (r.out, r.dx, r.dw_gate_up, r.dw_down))
+            par.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+
+
+def test_expert_ffn_world2_every_exchange_mode():
+    """moe.ExpertFFN over two ranks (NVLink peer memory) in every exchange
+    mode (sequential SM copies, SM copies beside the GEMMs, copy engines, copy
+    engines with the x dispatch split at local expert 2, returns from the
+    GEMM epilogues): all give the same bytes (the exchange moves rows and
+    changes no arithmetic), and those match the host restatement of the whole
+    two-rank layer step within the single-rank test's bound."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_layer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for pr in procs:
+        pr.join(timeout=60)
+    for r in range(2):
+        assert isinstance(res[r], dict), res[r]
+        base = res[r]["seq"]
+        for name, got in res[r].items():
+            for a, b, what in zip(base, got, ("out", "dx", "dw_gate_up", "dw_down")):
+                assert np.array_equal(a, b), (r, name, what)
+    E, H, I, k = 8, 256, 128, 2
+    wgu, wd, toks = _layer_problem(E, H, I, [300, 217], k)
+    b64 = lambda a: torch.from_numpy(a).to(torch.bfloat16).float().numpy().astype(np.float64)
+    x = np.concatenate([b64(t[0]) for t in toks])
+    dy = np.concatenate([b64(t[1]) for t in toks])
+    ids = np.concatenate([t[2] for t in toks])
+    p = np.concatenate([t[3] for t in toks]).astype(np.float64)
+    ref = _ffn_emulation(x, dy, b64(wgu), b64(wd), ids, p, E)
+    n0 = toks[0][0].shape[0]
+    for r, (lo, hi) in enumerate([(0, n0), (n0, x.shape[0])]):
+        out, dx, dwgu, dwd = res[r]["seq"]
+        El = E // 2
+        pairs = ((out, ref[True][0][lo:hi]), (dx, ref[True][1][lo:hi]),
+                 (dwgu, ref[True][2][r * El:(r + 1) * El]), (dwd, ref[True][3][r * El:(r + 1) * El]))
+        for (g, want), what in zip(pairs, ("out", "dx", "dw_gate_up", "dw_down")):
+            e = orc_mod.rel_frobenius(g.astype(np.float64), want)
+            assert e <= 3e-2, (r, what, e)

@@ -85,6 +85,28 @@ def _special_bf16(shape, gen, dev, scale=1.0):
     return x
 
 
+@pytest.mark.parametrize("shape,cuts", [((4192, 7168), (0, 1056, 4192)), ((352, 96), (0, 32, 160, 352)),
+                                        ((256, 64), (0, 0, 256))])
+def test_quantize_dual_rows_in_ranges_match_one_encode(mxg, cuda_dev, shape, cuts):
+    """mxg_quantize_dual_rows over consecutive row ranges (cuts at multiples
+    of 32 that split the 128-row tiles, an empty range included) writes the
+    same bytes as one quantize_dual of the whole tensor; a range outside the
+    tensor or off the 32-row grid is refused."""
+    gen = torch.Generator(device=cuda_dev).manual_seed(shape[0] * 3 + shape[1])
+    x = _special_bf16(shape, gen, cuda_dev)
+    q, s, qt, st = mxg.ops.quantize_dual(x)
+    out = mxg.ops.dual_outputs(x)
+    for t in out:
+        t.view(torch.uint8).fill_(0xA5)
+    for a, b in zip(cuts, cuts[1:]):
+        mxg.ops.quantize_dual_rows(x, a, b, out)
+    assert torch.equal(out[0].view(torch.uint8), q.view(torch.uint8)) and torch.equal(out[1], s)
+    assert torch.equal(out[2].view(torch.uint8), qt.view(torch.uint8)) and torch.equal(out[3], st)
+    for a, b in ((0, shape[0] + 32), (16, 32), (64, 32)):
+        with pytest.raises(mxg._lib.MxgError):
+            mxg.ops.quantize_dual_rows(x, a, b, out)
+
+
 @pytest.mark.parametrize("shape", [(32, 32), (64, 96), (4096, 7168), (160, 2048)])
 def test_quantize_dual_matches_separate_kernels(mxg, cuda_dev, shape):
     gen = torch.Generator(device=cuda_dev).manual_seed(shape[0] + shape[1])
