@@ -72,11 +72,6 @@ enum { MODE_FWD = 0, MODE_WGRAD = 1 };
 #ifndef MXG_WGRAD_BN
 #define MXG_WGRAD_BN 240
 #endif
-// wgrad epilogue stores: 0 = TMA bulk-tensor stores from the staging buffer,
-// 1 = plain coalesced stores read back from it (no wait on a bulk copy)
-#ifndef MXG_WGRAD_SYNC_STORE
-#define MXG_WGRAD_SYNC_STORE 0
-#endif
 #define MXG_WGRAD_EPI_WARPS_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_EPI_WARPS : 4)
 #define MXG_WGRAD_BN_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_BN : 240)
 template <int MODE>
@@ -481,7 +476,6 @@ struct GemmArgs {
   int stall_test;
   int fwd_tma_store;    // forward output row stride is 16-byte aligned: store via TMA
   int wgrad_tma_store;  // wgrad output row stride is 16-byte aligned: store via TMA
-  int wgrad_sync_store; // ... or through the warp's staging buffer with plain stores
   // forward, bf16, scatter mode (non-null scatter_bufs): output row q leaves
   // for row back_row[q] of buffer scatter_bufs[back_rank[q]] (this GPU's or
   // a peer's memory, plain stores), nothing is written to `out`
@@ -996,67 +990,6 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
             issue_store(cols_here == 32 ? &tmOut : &tmOut16, smem_u32(buf), f0, ti.b_row + c0, 0, false);
             slot ^= 1u;
           }
-        } else if (MODE == MODE_WGRAD && g.wgrad_sync_store) {
-          // row = lane.  Stage the 32 x 32 chunk row-major (16-byte pieces
-          // swizzled by row, so both the writes and the reads below are
-          // conflict-free), then read it back so that each store instruction
-          // writes whole row segments: fp32 4 rows x 128 B, bf16 8 rows x
-          // 64 B.  Nothing waits on an asynchronous copy: the buffer is free
-          // again after the warp's own reads.
-          const int r0 = ti.mb * kBM + qw * 32;
-          const int64_t base = (int64_t(ti.e) * g.n_out) * g.ldo + ti.n0 + c0;
-          __syncwarp();  // the previous chunk's reads of the buffer are done
-          if (f32) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              *reinterpret_cast<uint4*>(epi + lane * 128 + ((u ^ (lane & 7)) * 16)) =
-                  make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-            __syncwarp();
-            const int p = lane & 7, col = 4 * p;
-#pragma unroll
-            for (int it = 0; it < 8; ++it) {
-              const int rr = it * 4 + (lane >> 3);
-              const uint4 val = *reinterpret_cast<const uint4*>(epi + rr * 128 + ((p ^ (rr & 7)) * 16));
-              if (r0 + rr < g.n_out) {
-                float* o = reinterpret_cast<float*>(g.out) + base + int64_t(r0 + rr) * g.ldo + col;
-                if (col + 4 <= cols_here) {
-                  *reinterpret_cast<uint4*>(o) = val;
-                } else {
-                  const uint32_t w4[4] = {val.x, val.y, val.z, val.w};
-#pragma unroll
-                  for (int j = 0; j < 4; ++j)
-                    if (col + j < cols_here) o[j] = __uint_as_float(w4[j]);
-                }
-              }
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              *reinterpret_cast<uint4*>(epi + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) =
-                  make_uint4(pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
-                             pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
-                             pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
-                             pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
-            __syncwarp();
-            const int p = lane & 3, col = 8 * p;
-#pragma unroll
-            for (int it = 0; it < 4; ++it) {
-              const int rr = it * 8 + (lane >> 2);
-              const uint4 val = *reinterpret_cast<const uint4*>(epi + rr * 64 + ((p ^ ((rr >> 1) & 3)) * 16));
-              if (r0 + rr < g.n_out) {
-                __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + base + int64_t(r0 + rr) * g.ldo + col;
-                if (col + 8 <= cols_here) {
-                  *reinterpret_cast<uint4*>(o) = val;
-                } else {
-                  const uint32_t w4[4] = {val.x, val.y, val.z, val.w};
-#pragma unroll
-                  for (int j = 0; j < 8; ++j)
-                    if (col + j < cols_here)
-                      o[j] = __ushort_as_bfloat16(uint16_t((w4[j >> 1] >> (16 * (j & 1))) & 0xFFFFu));
-                }
-              }
-            }
-          }
         } else if (MODE == MODE_WGRAD && g.wgrad_tma_store && f32) {
           // row = lane; 32 fp32 columns (128 B rows, 128-byte swizzle) per
           // store from the warp's whole 4 KiB buffer, or 16 (64 B rows,
@@ -1483,13 +1416,7 @@ static int run_grouped(const Problem& P, const void* a_ptr, int64_t a_rows, cons
   ga.timeout_ns = stall > 0 ? uint64_t(stall) : kWaitLimitNs;
   ga.stall_test = stall > 0 ? 1 : 0;
   ga.fwd_tma_store = fwd_tma ? 1 : 0;
-#if MXG_WGRAD_SYNC_STORE
-  ga.wgrad_tma_store = 0;
-  ga.wgrad_sync_store = wgrad_tma ? 1 : 0;
-#else
   ga.wgrad_tma_store = wgrad_tma ? 1 : 0;
-  ga.wgrad_sync_store = 0;
-#endif
   ga.scatter_bufs = scatter ? scatter->bufs : nullptr;
   ga.back_rank = scatter ? scatter->back_rank : nullptr;
   ga.back_row = scatter ? scatter->back_row : nullptr;
