@@ -637,9 +637,11 @@ EP_EXPERTS, EP_TOKENS, EP_TOPK, EP_ZIPF = 256, 16384, 8, 1.1
 EP_LAUNCHES_PER_STEP = {"p2p": 4 + 20 + 8 + 2 + 3 + 2 + 2 + 2 + 2,
                         "nccl": 4 + 20 + 8 + 2 + 3 + 3 + 2 + 2}
 # the x dispatch is marked in parts: routing counts all-gathered (and any wait
-# for the slowest rank), plan (host gap and device tables), send, closing barrier
-EXCHANGE_SEGMENTS = ("x.counts", "x.plan", "x.send", "dispatch_x", "wait_x_rest", "dispatch_dy", "return_y",
-                     "return_dx")
+# for the slowest rank), plan (host gap and device tables), send, closing barrier;
+# with a comm stream the main stream's waits for it are marked too (the rest of
+# a split x dispatch, dy, the returns): exchange time not hidden behind kernels
+EXCHANGE_SEGMENTS = ("x.counts", "x.plan", "x.send", "dispatch_x", "wait_x_rest", "dispatch_dy", "wait_dy",
+                     "return_y", "return_dx", "wait_returns")
 
 
 def rank0_like_popularity(seed, world=8):

@@ -220,6 +220,8 @@ class ExpertFFN:
             if comm is None:
                 self._mark("return_y")
         main.wait_event(dy_ready)
+        if comm is not None:
+            self._mark("wait_dy")                           # the dy exchange not yet hidden
         dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
         self._mark("quantize_dy")
         with ops.gemm_sm_limit(self.gemm_sms):             # beside the y return
@@ -253,6 +255,7 @@ class ExpertFFN:
             # this wait (the next dispatch syncs on main before the comm
             # stream waits on main), so no record_stream is needed.
             main.wait_stream(comm)
+            self._mark("wait_returns")                      # the returns not yet hidden
         out = ep.combine_finish(ret, plan, probs)
         dx = ep.combine_finish(ret_dx, plan, None) if ret_dx is not None else None
         self._mark("combine")
