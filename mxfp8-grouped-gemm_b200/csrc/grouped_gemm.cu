@@ -72,12 +72,18 @@ enum { MODE_FWD = 0, MODE_WGRAD = 1 };
 #ifndef MXG_WGRAD_BN
 #define MXG_WGRAD_BN 240
 #endif
+// staging bytes per wgrad epilogue warp: 4096 (32 fp32 columns, 128-byte rows
+// per store) or 2048 (16 fp32 / 32 bf16 columns, 64-byte rows per store)
+#ifndef MXG_WGRAD_EPI_SLOT
+#define MXG_WGRAD_EPI_SLOT 4096
+#endif
 #define MXG_WGRAD_EPI_WARPS_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_EPI_WARPS : 4)
 #define MXG_WGRAD_BN_FOR(m) ((m) == MODE_WGRAD ? MXG_WGRAD_BN : 240)
 template <int MODE>
 struct Cfg {
   static constexpr int kStages = 6;
   static constexpr int kEpiWarps = MXG_WGRAD_EPI_WARPS_FOR(MODE);
+  static constexpr int kEpiBytes = MODE == MODE_WGRAD ? MXG_WGRAD_EPI_SLOT : 4096;
   static constexpr int kThreads = 32 * (kEpiWarps + 2);
   static constexpr int kBN = MXG_WGRAD_BN_FOR(MODE);            // max B rows per pair tile
   static constexpr int kBHalf = kBN / 2;                       // B rows each CTA loads
@@ -486,14 +492,14 @@ struct GemmArgs {
   int64_t scatter_rows;
 };
 
-template <int S, int EW, int BB>
+template <int S, int EW, int BB, int EB>
 struct __align__(1024) SmemT {
   static constexpr int kStages = S;
   uint8_t a[S][kABytes];
   uint8_t b[S][BB];
   uint8_t sfa[S][kSfaBytes];
   uint8_t sfb[S][kSfbBytes];
-  alignas(1024) uint8_t epi[EW][4096];  // per epilogue warp: 4 KiB staging (two 2 KiB slots), swizzled
+  alignas(1024) uint8_t epi[EW][EB];    // per epilogue warp: staging (4 KiB: two 2 KiB slots), swizzled
   uint64_t full[S];            // leader: both CTAs' loads of the stage landed
   uint64_t empty[S];           // each CTA: the pair MMA finished reading the stage
   uint64_t acc_full[2];        // each CTA: accumulator buffer complete
@@ -508,7 +514,7 @@ struct __align__(1024) SmemT {
   int tile_start[MXG_MAX_GROUPS + 1];
 };
 template <int MODE>
-using SmemOf = SmemT<Cfg<MODE>::kStages, Cfg<MODE>::kEpiWarps, Cfg<MODE>::kBBytes>;
+using SmemOf = SmemT<Cfg<MODE>::kStages, Cfg<MODE>::kEpiWarps, Cfg<MODE>::kBBytes, Cfg<MODE>::kEpiBytes>;
 template <int MODE>
 constexpr size_t smem_bytes() { return sizeof(SmemOf<MODE>) + 1024; }
 // swizzled tiles must start on 1024-byte boundaries (the swizzle pattern is
@@ -997,6 +1003,24 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           // store clips at the tensor edge.  Half as many store requests as
           // 64-byte rows through two 2 KiB slots, which measured slower.
           const int r0 = ti.mb * kBM + qw * 32;
+          if constexpr (Cfg<MODE>::kEpiBytes < 4096) {  // 2 KiB slot: 16 columns (64-byte rows) per store
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              if (16 * hh < cols_here) {
+                if (epi_pending) {
+                  if (lane == 0) bulk_wait_group_read0();
+                  __syncwarp();
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                  *reinterpret_cast<uint4*>(epi + lane * 64 + ((u ^ ((lane >> 1) & 3)) * 16)) =
+                      make_uint4(v[16 * hh + 4 * u], v[16 * hh + 4 * u + 1], v[16 * hh + 4 * u + 2],
+                                 v[16 * hh + 4 * u + 3]);
+                issue_store(&tmOut16, smem_u32(epi), ti.n0 + c0 + 16 * hh, r0, ti.e, true);
+              }
+            }
+            return;
+          }
           if (epi_pending) {
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
@@ -1023,7 +1047,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           // rows (unswizzled); the tensor edge clips every store.
           const int r0 = ti.mb * kBM + qw * 32;
           const int pair0 = c0 & ~63;
-          const bool paired = pair0 + 64 <= ti.nlen;
+          const bool paired = Cfg<MODE>::kEpiBytes >= 4096 && pair0 + 64 <= ti.nlen;
           auto pack8 = [&](int u) {
             return make_uint4(pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
                               pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),

@@ -51,7 +51,8 @@ class ExpertFFN:
     def __init__(self, ep: ExpertParallel, w_gate_up: torch.Tensor, w_down: torch.Tensor,
                  comm_stream: torch.cuda.Stream | None = None, reserve_sms: int = 0,
                  wgrad_dtype: torch.dtype = torch.bfloat16, compute_dx: bool = True,
-                 copy_engines: bool = False, fused_return: bool = False, split_experts: int = 0):
+                 copy_engines: bool = False, fused_return: bool = False, split_experts: int = 0,
+                 exchanges_after_encodes: bool = False):
         """With a comm stream, the dy dispatch and the returns run beside the
         GEMMs.  reserve_sms > 0 keeps that many SMs free of GEMM blocks while
         they do, and runs the peer copies only there.  wgrad_dtype is the
@@ -71,7 +72,11 @@ class ExpertFFN:
         of every rank's first split_experts local experts with the SM kernel
         and the rest by copy-engine runs on the comm stream, while this rank
         encodes and multiplies its first split_experts groups; 0: one
-        dispatch."""
+        dispatch.  With a comm stream each exchange starts as soon as its data
+        is ready; exchanges_after_encodes: only once the encode in front of the
+        next GEMM has been issued, so the copies run beside GEMMs and not
+        beside the HBM-bound encodes (on 2 B200s no faster: the encodes took
+        the same time either way)."""
         if wgrad_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("wgrad_dtype must be torch.bfloat16 or torch.float32")
         self.wgrad_dtype = wgrad_dtype
@@ -99,6 +104,7 @@ class ExpertFFN:
         self.comm = comm_stream
         self.ce = bool(copy_engines and comm_stream is not None)
         self.fused_return = bool(fused_return and ep.transport == "p2p")
+        self.late = bool(exchanges_after_encodes)
         self.split = int(split_experts) if (self.ce and ep.transport == "p2p" and 0 < split_experts < E) else 0
         self.reserve = reserve_sms if comm_stream is not None else 0
         if self.reserve:
@@ -165,27 +171,39 @@ class ExpertFFN:
         self._plan = plan
         offs = plan.group_rows
         self._mark("dispatch_x")
-        if comm is not None:
-            comm.wait_stream(main)
-        with side():
-            if plan.split:
-                ep.dispatch_rest(plan)                      # the other experts' rows, copy engines
-                x_rest = torch.cuda.Event()
-                x_rest.record()
-            dy_local = ep.dispatch_like(dy, plan, copy_engines=self.ce)
-            dy_ready = torch.cuda.Event()
-            dy_ready.record()
-        if comm is None:
-            self._mark("dispatch_dy")
+        # with a comm stream, an exchange starts as soon as its data is ready,
+        # or (self.late) once the encode in front of the next GEMM is issued
+        late = comm is not None and self.late
+
+        def on_side(fn):
+            if comm is not None:
+                comm.wait_stream(main)
+            with side():
+                r = fn()
+                ev = torch.cuda.Event()
+                ev.record()
+            return r, ev
+
+        def send_dy():
+            r, ev = on_side(lambda: ep.dispatch_like(dy, plan, copy_engines=self.ce))
+            if comm is None:
+                self._mark("dispatch_dy")
+            return r, ev
+
         if plan.split:
             # groups [0, h) while the rest arrive; the encodes write the
             # bytes one whole-tensor encode would
+            if not late:
+                _, x_rest = on_side(lambda: ep.dispatch_rest(plan))   # the other experts' rows
+                dy_local, dy_ready = send_dy()
             h, M = plan.split, x_local.shape[0]
             ra = int(sum(plan.group_rows_host[:h]))
             xo = ops.dual_outputs(x_local)
             xq, xs, ia_g, ias_g = xo
             gu = torch.empty(M, 2 * self.I, dtype=torch.bfloat16, device=x_local.device)
             ops.quantize_dual_rows(x_local, 0, ra, xo)
+            if late:
+                _, x_rest = on_side(lambda: ep.dispatch_rest(plan))
             self._mark("quantize_x")
             with ops.gemm_sm_limit(self.gemm_sms):
                 self._fwd_groups((xq, xs), self.wgu, offs, 0, h, 0, ra, gu)
@@ -193,11 +211,17 @@ class ExpertFFN:
             main.wait_event(x_rest)
             self._mark("wait_x_rest")
             ops.quantize_dual_rows(x_local, ra, M, xo)
+            if late:
+                dy_local, dy_ready = send_dy()
             self._mark("quantize_x")
             with ops.gemm_sm_limit(self.gemm_sms):
                 self._fwd_groups((xq, xs), self.wgu, offs, h, self.E, ra, M, gu)
         else:
+            if not late:
+                dy_local, dy_ready = send_dy()
             xq, xs, ia_g, ias_g = ops.quantize_dual(x_local)   # fwd operand + gate/up wgrad operand
+            if late:
+                dy_local, dy_ready = send_dy()
             self._mark("quantize_x")
             with ops.gemm_sm_limit(self.gemm_sms):             # beside the dy exchange
                 gu = self._fwd((xq, xs), self.wgu, offs)
@@ -213,16 +237,16 @@ class ExpertFFN:
         else:
             y_local = self._fwd((hq, hs), self.wd, offs)
             self._mark("fwd_down")
-            if comm is not None:
-                comm.wait_stream(main)
-            with side():
-                ret = ep.combine_send(y_local, plan, copy_engines=self.ce)
-            if comm is None:
-                self._mark("return_y")
+            if not late:
+                ret, _ = on_side(lambda: ep.combine_send(y_local, plan, copy_engines=self.ce))
+                if comm is None:
+                    self._mark("return_y")
         main.wait_event(dy_ready)
         if comm is not None:
             self._mark("wait_dy")                           # the dy exchange not yet hidden
         dyq, dys, go_d, gos_d = ops.quantize_dual(dy_local)  # dgrad operand + down wgrad operand
+        if late and not self.fused_return:                  # the y return beside the down dgrad/wgrad
+            ret, _ = on_side(lambda: ep.combine_send(y_local, plan, copy_engines=self.ce))
         self._mark("quantize_dy")
         with ops.gemm_sm_limit(self.gemm_sms):             # beside the y return
             dh = self._fwd((dyq, dys), self.wdt, offs)
@@ -241,10 +265,7 @@ class ExpertFFN:
             with ops.gemm_sm_limit(self.gemm_sms):
                 dx_local = self._fwd((dgq, dgs), self.wgut, offs)
             self._mark("dgrad_gate_up")
-            if comm is not None:
-                comm.wait_stream(main)
-            with side():
-                ret_dx = ep.combine_send(dx_local, plan, buffer="ret_dx", copy_engines=self.ce)
+            ret_dx, _ = on_side(lambda: ep.combine_send(dx_local, plan, buffer="ret_dx", copy_engines=self.ce))
             if comm is None:
                 self._mark("return_dx")
         with ops.gemm_sm_limit(self.gemm_sms):             # beside the dx return
