@@ -38,6 +38,19 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// cvt_e4m3x2(lo * f, hi * f), the two products from one packed f32x2
+// multiply (each lane rounds exactly as a scalar multiply: the same bits in
+// half the multiply instructions).
+__device__ __forceinline__ uint32_t cvt_scaled_e4m3x2(float lo, float hi, float f) {
+  uint64_t ab, ff, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ab) : "f"(lo), "f"(hi));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ff) : "f"(f));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(ab), "l"(ff));
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+  return cvt_e4m3x2(a, b);
+}
+
 __device__ __forceinline__ uint32_t amax2(uint32_t w) {
   const uint32_t a = w & 0x7FFFu, b = (w >> 16) & 0x7FFFu;
   return a > b ? a : b;

@@ -60,10 +60,10 @@ __global__ void __launch_bounds__(256) quant_rowwise_kernel(const uint4* __restr
       m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
       const uint32_t b = rceil_byte(m);
       const float f = descale_of(b);
-      uint32_t c0 = cvt_e4m3x2(bf16_lo(v[u].x) * f, bf16_hi(v[u].x) * f);
-      uint32_t c1 = cvt_e4m3x2(bf16_lo(v[u].y) * f, bf16_hi(v[u].y) * f);
-      uint32_t c2 = cvt_e4m3x2(bf16_lo(v[u].z) * f, bf16_hi(v[u].z) * f);
-      uint32_t c3 = cvt_e4m3x2(bf16_lo(v[u].w) * f, bf16_hi(v[u].w) * f);
+      uint32_t c0 = cvt_scaled_e4m3x2(bf16_lo(v[u].x), bf16_hi(v[u].x), f);
+      uint32_t c1 = cvt_scaled_e4m3x2(bf16_lo(v[u].y), bf16_hi(v[u].y), f);
+      uint32_t c2 = cvt_scaled_e4m3x2(bf16_lo(v[u].z), bf16_hi(v[u].z), f);
+      uint32_t c3 = cvt_scaled_e4m3x2(bf16_lo(v[u].w), bf16_hi(v[u].w), f);
       uint32_t lo = c0 | (c1 << 16), hi = c2 | (c3 << 16);
       if (b == 255u) {
         const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
@@ -116,10 +116,10 @@ __global__ void __launch_bounds__(kColThreads) quant_colwise_kernel(
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     // rows 4j .. 4j+3 of column c (low halves) and column c+1 (high halves)
-    uint32_t a01 = cvt_e4m3x2(bf16_lo(w[4 * j]) * f0, bf16_lo(w[4 * j + 1]) * f0);
-    uint32_t a23 = cvt_e4m3x2(bf16_lo(w[4 * j + 2]) * f0, bf16_lo(w[4 * j + 3]) * f0);
-    uint32_t b01 = cvt_e4m3x2(bf16_hi(w[4 * j]) * f1, bf16_hi(w[4 * j + 1]) * f1);
-    uint32_t b23 = cvt_e4m3x2(bf16_hi(w[4 * j + 2]) * f1, bf16_hi(w[4 * j + 3]) * f1);
+    uint32_t a01 = cvt_scaled_e4m3x2(bf16_lo(w[4 * j]), bf16_lo(w[4 * j + 1]), f0);
+    uint32_t a23 = cvt_scaled_e4m3x2(bf16_lo(w[4 * j + 2]), bf16_lo(w[4 * j + 3]), f0);
+    uint32_t b01 = cvt_scaled_e4m3x2(bf16_hi(w[4 * j]), bf16_hi(w[4 * j + 1]), f1);
+    uint32_t b23 = cvt_scaled_e4m3x2(bf16_hi(w[4 * j + 2]), bf16_hi(w[4 * j + 3]), f1);
     out0[j] = a01 | (a23 << 16);
     out1[j] = b01 | (b23 << 16);
   }
@@ -208,10 +208,10 @@ __device__ __forceinline__ void encode_row_chunk(const DualArgs& a, uint4 v, int
   const uint32_t m = halves_max(m2);
   const uint32_t b = rceil_byte(m);
   const float f = descale_of(b);
-  uint32_t c0 = cvt_e4m3x2(bf16_lo(v.x) * f, bf16_hi(v.x) * f);
-  uint32_t c1 = cvt_e4m3x2(bf16_lo(v.y) * f, bf16_hi(v.y) * f);
-  uint32_t c2 = cvt_e4m3x2(bf16_lo(v.z) * f, bf16_hi(v.z) * f);
-  uint32_t c3 = cvt_e4m3x2(bf16_lo(v.w) * f, bf16_hi(v.w) * f);
+  uint32_t c0 = cvt_scaled_e4m3x2(bf16_lo(v.x), bf16_hi(v.x), f);
+  uint32_t c1 = cvt_scaled_e4m3x2(bf16_lo(v.y), bf16_hi(v.y), f);
+  uint32_t c2 = cvt_scaled_e4m3x2(bf16_lo(v.z), bf16_hi(v.z), f);
+  uint32_t c3 = cvt_scaled_e4m3x2(bf16_lo(v.w), bf16_hi(v.w), f);
   uint32_t lo = c0 | (c1 << 16), hi = c2 | (c3 << 16);
   if (b == 255u) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -279,10 +279,10 @@ __device__ __forceinline__ void dual_column_pass(const DualArgs& a, const uint32
     uint32_t o0[4], o1[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t a01 = cvt_e4m3x2(bf16_lo(w[4 * j]) * f0, bf16_lo(w[4 * j + 1]) * f0);
-      const uint32_t a23 = cvt_e4m3x2(bf16_lo(w[4 * j + 2]) * f0, bf16_lo(w[4 * j + 3]) * f0);
-      const uint32_t b01 = cvt_e4m3x2(bf16_hi(w[4 * j]) * f1, bf16_hi(w[4 * j + 1]) * f1);
-      const uint32_t b23 = cvt_e4m3x2(bf16_hi(w[4 * j + 2]) * f1, bf16_hi(w[4 * j + 3]) * f1);
+      const uint32_t a01 = cvt_scaled_e4m3x2(bf16_lo(w[4 * j]), bf16_lo(w[4 * j + 1]), f0);
+      const uint32_t a23 = cvt_scaled_e4m3x2(bf16_lo(w[4 * j + 2]), bf16_lo(w[4 * j + 3]), f0);
+      const uint32_t b01 = cvt_scaled_e4m3x2(bf16_hi(w[4 * j]), bf16_hi(w[4 * j + 1]), f1);
+      const uint32_t b23 = cvt_scaled_e4m3x2(bf16_hi(w[4 * j + 2]), bf16_hi(w[4 * j + 3]), f1);
       o0[j] = a01 | (a23 << 16);
       o1[j] = b01 | (b23 << 16);
       if (b0 == 255u || b1 == 255u) {
