@@ -664,7 +664,8 @@ class EpLayerBench:
 
     def __init__(self, rank, world, seed=0, placement="balanced", overlap=True, tokens=EP_TOKENS,
                  transport="auto", p2p_blocks=0, reserve_sms=0, wgrad_dtype="bf16", experts=EP_EXPERTS,
-                 logp=None, compute_dx=True, copy_engines=False, fused_return=True, split_x=0, late=False):
+                 logp=None, compute_dx=True, copy_engines=False, fused_return=True, split_x=0, late=False,
+                 ce_streams=-1):
         m = pkg()
         W = m.workloads
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -677,7 +678,7 @@ class EpLayerBench:
         self.slot = slot
         self.placement = placement if world > 1 else "single"
         self.ep = m.ExpertParallel(experts, placement=slot, transport=transport,
-                                   p2p_max_blocks=p2p_blocks)
+                                   p2p_max_blocks=p2p_blocks, ce_streams=ce_streams)
         g = torch.Generator(device=dev).manual_seed(seed * 1000 + 17 + rank)
         self.x = torch.randn(tokens, HIDDEN, generator=g, device=dev, dtype=torch.bfloat16)
         self.dy = (torch.randn(tokens, HIDDEN, generator=g, device=dev) * 1e-2).to(torch.bfloat16)
@@ -972,7 +973,7 @@ def run_ep_mxg(args, rank, world, local):
                       transport=args.transport, p2p_blocks=args.p2p_blocks, reserve_sms=args.reserve_sms,
                       wgrad_dtype=args.ep_wgrad_dtype, compute_dx=not args.no_dx,
                       copy_engines=args.copy_engines, fused_return=not args.no_fused_return,
-                      split_x=args.split_x, late=args.exchange_late)
+                      split_x=args.split_x, late=args.exchange_late, ce_streams=args.ce_streams)
     with ClockSampler(local) as clk:
         r = measure_ep_layer(lb, world, args.steps, args.warmup)
     e2e = None
@@ -1006,7 +1007,7 @@ def run_ep_mxg(args, rank, world, local):
            "data": "synthetic",
            "config": ep_config(world, args.placement, args.overlap, r["transport"], r["reserve_sms"],
                                args.ep_wgrad_dtype, args.seed, not args.no_dx, args.copy_engines,
-                               not args.no_fused_return, args.split_x, args.exchange_late),
+                               not args.no_fused_return, args.split_x, args.exchange_late, args.ce_streams),
            "roofline": r["roofline"], "layer": {k: r[k] for k in (
                "ms_per_step_this_rank", "flops_per_step_all_ranks", "recv_rows_per_rank",
                "padded_rows_this_rank", "segments_ms_rank0", "exposed_exchange_ms_rank0", "gemm_ms_rank0",
@@ -1045,7 +1046,7 @@ def ep_flops(rows, dx=True):
 
 
 def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, seed, dx, copy_engines=False,
-              fused=True, split_x=0, late=False):
+              fused=True, split_x=0, late=False, ce_streams=-1):
     """The config object of a config-4 line (the reference arm prints the same)."""
     rows, padded = ep_routing_stats(world, seed, placement)
     flops_rank = ep_flops(rows[0], dx)
@@ -1061,6 +1062,8 @@ def ep_config(world, placement, overlap, transport, reserve_sms, wgrad_dtype, se
             "returns": "from the GEMM epilogues" if (fused and transport == "p2p") else "separate exchange",
             "exchange_start": ("after the encode in front of the next GEMM" if late else
                                "as soon as its data is ready") if overlap else "in sequence",
+            "copy_engine_streams": ((world - 1 if ce_streams < 0 else min(ce_streams, world))
+                                    if (overlap and copy_engines and transport == "p2p") else 0),
             "x_dispatch": (f"split: local experts [0, {split_x}) by the SM kernel, the rest by the copy engines "
                            f"beside their encode and GEMM"
                            if (split_x and overlap and copy_engines and transport == "p2p"
@@ -1278,7 +1281,7 @@ def run_reference_layer(args, world):
                                "nccl" if args.transport == "nccl" else "p2p",
                                args.reserve_sms if args.overlap else 0, args.ep_wgrad_dtype, args.seed,
                                not args.no_dx, args.copy_engines, not args.no_fused_return, args.split_x,
-                               args.exchange_late),
+                               args.exchange_late, args.ce_streams),
            "cpu_baseline": {"value": round(v, 4), "unit": "TFLOPS", "cores": torch.get_num_threads(),
                             "kind": "port", "sample": sample},
            "e2e": {"value": round(v, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1367,6 +1370,9 @@ def main():
     ap.add_argument("--split-x", type=int, default=0,
                     help="EP layer with --exchange ce: the x dispatch sends local experts [0, H) of every "
                          "rank first and the rest by the copy engines beside their encode and GEMM (0: one pass)")
+    ap.add_argument("--ce-streams", type=int, default=-1,
+                    help="EP layer, copy-engine exchanges: streams the runs are spread over, by destination "
+                         "rank (-1: one per peer; 1: all runs on the side stream)")
     ap.add_argument("--exchange-late", action="store_true",
                     help="EP layer with a side stream: start each exchange only after the encode in front of "
                          "the next GEMM (default: as soon as its data is ready)")

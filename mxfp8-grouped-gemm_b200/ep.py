@@ -355,12 +355,16 @@ class ExpertParallel:
     """Dispatch/combine of routed token rows over a process group."""
 
     def __init__(self, num_experts: int, group=None, pad: int = 32, ops=None, placement=None,
-                 transport: str = "auto", max_tokens: int = 0, p2p_max_blocks: int = 0):
+                 transport: str = "auto", max_tokens: int = 0, p2p_max_blocks: int = 0,
+                 ce_streams: int = -1):
         """transport: "p2p" (rows written straight into the owners' buffers
         over NVLink, ranks of one node), "nccl" (all_to_all_single), or "auto"
         (p2p on CUDA with more than one rank).  max_tokens sizes the p2p
         receive buffers for batches up to that many tokens per rank (they
-        grow on demand, collectively, when a larger batch arrives)."""
+        grow on demand, collectively, when a larger batch arrives).
+        ce_streams: copy-engine exchanges issue the runs of each destination
+        rank on one of this many streams (-1: one per peer), so several copy
+        engines move rows at once; 1: every run on the calling stream."""
         self.group = group
         self.world = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -389,6 +393,36 @@ class ExpertParallel:
         self.capacity = {}       # name -> rows
         self._flag = None
         self.marker = None       # optional callable(name): a timing mark on the current stream
+        self.ce_streams = (self.world - 1 if ce_streams < 0 else ce_streams)
+        self._ce = []            # the copy-engine streams, created on first use
+
+    def _copy_runs(self, src, runs, peer_host, rows):
+        """Copy-engine runs (grouped by destination rank, as copy_run_tables
+        orders them): each destination's runs on one of the copy-engine
+        streams, which start after the calling stream's preceding work and
+        which the calling stream then waits for."""
+        k = min(self.ce_streams, self.world)
+        dst = runs[3]
+        if k <= 1 or dst.size == 0:
+            self.p2p.copy_runs(src, runs, peer_host, rows)
+            return
+        cur = torch.cuda.current_stream(src.device)
+        if len(self._ce) < k or self._ce[0].device != src.device:
+            self._ce = [torch.cuda.Stream(src.device) for _ in range(k)]
+        cuts = np.concatenate([[0], np.flatnonzero(np.diff(dst)) + 1, [dst.size]])
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        used = []
+        for i, (lo, hi) in enumerate(zip(cuts[:-1], cuts[1:])):
+            st = self._ce[i % k]
+            if i < k:
+                st.wait_event(ready)
+                src.record_stream(st)          # read there: keep the block until those copies ran
+                used.append(st)
+            with torch.cuda.stream(st):
+                self.p2p.copy_runs(src, tuple(a[lo:hi] for a in runs), peer_host, rows)
+        for st in used:
+            cur.wait_stream(st)
 
     def _mark(self, name):
         if self.marker is not None:
@@ -570,7 +604,7 @@ class ExpertParallel:
         send.record_stream(torch.cuda.current_stream(send.device))
         plan.later = None
         rows, _ = self.capacity["x"]
-        self.p2p.copy_runs(send, plan.runs_later, self.buffers["x"].ptrs_host, rows)
+        self._copy_runs(send, plan.runs_later, self.buffers["x"].ptrs_host, rows)
         self._barrier(send.device)
 
     def dispatch_like(self, x: torch.Tensor, plan: DispatchPlan, buffer: str = "dy",
@@ -599,7 +633,7 @@ class ExpertParallel:
                 # out again before they have read it
                 send.record_stream(torch.cuda.current_stream(send.device))
             plan.pregathered = plan.pregathered_src = None
-            self.p2p.copy_runs(send, plan.runs_dispatch, buf.ptrs_host, rows)
+            self._copy_runs(send, plan.runs_dispatch, buf.ptrs_host, rows)
             self._barrier(x.device)
             return local
         if plan.back_rank is not None:
@@ -648,7 +682,7 @@ class ExpertParallel:
                 self._barrier(y_local.device)   # as in dispatch_like: nobody waits for this rank
                 raise ValueError("combine rows must have the dispatched rows' size")
             if copy_engines:
-                self.p2p.copy_runs(y_local, plan.runs_return, buf.ptrs_host, rows)
+                self._copy_runs(y_local, plan.runs_return, buf.ptrs_host, rows)
             else:
                 self.p2p.ret(y_local, plan.ret_order, plan.back_rank, plan.back_row, buf.ptrs, rows,
                              self.p2p_max_blocks)

@@ -492,11 +492,13 @@ def test_expert_ffn_world1(mxg, cuda_dev, wgrad_dtype):
         assert eq <= 3e-2 and ef <= 0.12, (name, eq, ef)
 
 
-_LAYER_MODES = {  # name -> (comm stream, copy engines, fused returns, split experts, exchanges after encodes)
-    "seq": (False, False, False, 0, False), "sm": (True, False, False, 0, False),
-    "ce": (True, True, False, 0, False), "ce_late": (True, True, False, 0, True),
-    "ce_split": (True, True, False, 2, False), "ce_split_late": (True, True, False, 2, True),
-    "fused": (True, False, True, 0, False)}
+_LAYER_MODES = {  # name -> (comm stream, copy engines, fused returns, split experts, exchanges after
+    #                  encodes, copy-engine streams)
+    "seq": (False, False, False, 0, False, -1), "sm": (True, False, False, 0, False, -1),
+    "ce": (True, True, False, 0, False, -1), "ce_late": (True, True, False, 0, True, -1),
+    "ce_2streams": (True, True, False, 0, False, 2), "ce_split": (True, True, False, 2, False, -1),
+    "ce_split_late": (True, True, False, 2, True, -1), "ce_split_2streams": (True, True, False, 2, False, 2),
+    "fused": (True, False, True, 0, False, -1)}
 
 
 def _layer_problem(E, H, I, ns, k):
@@ -528,8 +530,8 @@ def _layer_worker(rank, world, port, q):
         x, dy, ids, p = toks[rank]
         bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)
         res = {}
-        for name, (side, ce, fused, split, late) in _LAYER_MODES.items():
-            par = mxg.ExpertParallel(E, transport="p2p")
+        for name, (side, ce, fused, split, late, streams) in _LAYER_MODES.items():
+            par = mxg.ExpertParallel(E, transport="p2p", ce_streams=streams)
             layer = mxg.moe.ExpertFFN(par, bf(wgu[rank * El:(rank + 1) * El]), bf(wd[rank * El:(rank + 1) * El]),
                                       comm_stream=torch.cuda.Stream() if side else None, copy_engines=ce,
                                       fused_return=fused, split_experts=split, exchanges_after_encodes=late)
@@ -551,8 +553,8 @@ def test_expert_ffn_world2_every_exchange_mode():
     """moe.ExpertFFN over two ranks (NVLink peer memory) in every exchange
     mode (sequential SM copies, SM copies beside the GEMMs, copy engines, copy
     engines with the x dispatch split at local expert 2, each copy-engine
-    mode with its exchanges started after the encodes too, returns from the
-    GEMM epilogues): all give the same bytes (the exchange moves rows and
+    mode with its exchanges started after the encodes too and with its runs
+    spread over two streams, returns from the GEMM epilogues): all give the same bytes (the exchange moves rows and
     changes no arithmetic), and those match the host restatement of the whole
     two-rank layer step within the single-rank test's bound."""
     if torch.cuda.device_count() < 2:
