@@ -288,3 +288,26 @@ def test_split_dispatch_runs_cover_the_later_slots_once(world):
                 bufs[d][b:b + c] = send[a:a + c]
         for d in range(world):
             assert np.array_equal(bufs[d], out[d][0])
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_copy_run_tables_group_runs_by_destination(world):
+    """The copy-engine exchanges put each destination rank's runs on a
+    stream of its own by cutting the run tables where the destination
+    changes: every destination must form one contiguous block, in the
+    rotated order me+1, me+2, ... (dispatch, the split's later runs and the
+    return alike)."""
+    from conftest import load_pkg
+    ep = load_pkg().ep
+    rng = np.random.default_rng(world)
+    E = 4 * world
+    C = rng.integers(0, 40, size=(world, E))
+    C[rng.random((world, E)) < 0.4] = 0
+    for me in range(world):
+        tables = list(ep.copy_run_tables(C, me, 32)) + [ep.copy_run_tables(C, me, 32, first_slot=2)[0]]
+        for (_, _, rows, dst) in tables:
+            assert rows.min(initial=1) > 0
+            blocks = [int(d) for i, d in enumerate(dst) if i == 0 or dst[i - 1] != d]
+            assert len(blocks) == len(set(blocks))
+            rot = [(d - me - 1) % world for d in blocks]
+            assert rot == sorted(rot)
