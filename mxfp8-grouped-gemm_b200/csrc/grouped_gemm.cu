@@ -317,7 +317,7 @@ __device__ __forceinline__ uint32_t scale_word(const uint8_t* srow, const uint32
   return word;
 }
 
-__global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
+__device__ __forceinline__ void pack_rows(const PackArgs& p, int bid, int nblk) {
   __shared__ int ustart[MXG_MAX_GROUPS + 1];  // B side: first unit of each group
   MetaView mv{const_cast<int*>(p.meta), p.E};
   const int mbp = ceil_div(p.n_out, 2 * kBM);
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
   const int ks = int(threadIdx.x) / tpu, t = int(threadIdx.x) % tpu;
   const int half = t >> 5, q = t & 31;
   const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+  for (int u = bid; u < units; u += nblk) {
     int e, blk;
     if (p.side == 0) {
       e = u / (2 * mbp);
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(256) pack_scales_kernel(PackArgs p) {
 // Chunk-parallel variant: one block per chunk at a time, thread r reads the
 // four bytes of row r.  Faster than the row walk when the scale rows are not
 // word aligned (the wgrad's token-contiguous scales, M/32 bytes per row).
-__global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
+__device__ __forceinline__ void pack_chunks(const PackArgs& p, int bid, int nblk) {
   __shared__ int base_s[MXG_MAX_GROUPS + 1];
   MetaView mv{const_cast<int*>(p.meta), p.E};
   const int* base = p.side == 0 ? mv.g_asf() : mv.g_bsf();
@@ -418,8 +418,8 @@ __global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
   const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
   const int total = base_s[p.E] * halves;
   const int lane = threadIdx.x & 31;
-  const int warps = int(gridDim.x * blockDim.x) >> 5;
-  for (int item = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < total; item += warps) {
+  const int warps = int(nblk * blockDim.x) >> 5;
+  for (int item = int(bid * blockDim.x + threadIdx.x) >> 5; item < total; item += warps) {
     const int c = item / halves, half = item - c * halves;
     int lo = 0, hi = p.E - 1;
     while (lo < hi) {
@@ -469,6 +469,26 @@ __global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackArgs p) {
     *reinterpret_cast<uint4*>(p.dst + int64_t(c) * chunk_bytes + half * 512 + lane * 16) =
         make_uint4(w[0], w[1], w[2], w[3]);
   }
+}
+
+// Both operands' scales in one launch: blocks [0, blocks0) pack the A side,
+// the rest the B side, so the two run side by side with one kernel boundary
+// between the scheduler and the GEMM instead of two.
+struct PackPair {
+  PackArgs side[2];
+  int blocks0;
+};
+
+__global__ void __launch_bounds__(256) pack_scales_kernel(PackPair pp) {
+  const bool second = int(blockIdx.x) >= pp.blocks0;
+  pack_rows(pp.side[second ? 1 : 0], second ? int(blockIdx.x) - pp.blocks0 : int(blockIdx.x),
+            second ? int(gridDim.x) - pp.blocks0 : pp.blocks0);
+}
+
+__global__ void __launch_bounds__(256) pack_scales_chunk_kernel(PackPair pp) {
+  const bool second = int(blockIdx.x) >= pp.blocks0;
+  pack_chunks(pp.side[second ? 1 : 0], second ? int(blockIdx.x) - pp.blocks0 : int(blockIdx.x),
+              second ? int(gridDim.x) - pp.blocks0 : pp.blocks0);
 }
 
 
@@ -1354,16 +1374,15 @@ static int prepare_grouped(const Problem& P, const void* a_sc, const void* b_sc,
   if (P.mode == MODE_FWD) {  // K/32-byte scale rows: word-aligned row walks
     // 256 threads per unit: 8 k-split groups of a 128-row A unit, 4 of a
     // 256-row B unit
-    pack_scales_kernel<<<std::max(1, std::min(a_units, sms * 16)), 256, 0, stream>>>(pa);
-    pack_scales_kernel<<<sms * 8, 256, 0, stream>>>(pb);
+    const int ga = std::max(1, std::min(a_units, sms * 16));
+    pack_scales_kernel<<<ga + sms * 8, 256, 0, stream>>>(PackPair{{pa, pb}, ga});
   } else {
     // about one chunk half per warp (the chunk counts are bounded by the
     // workspace layout), so each warp's loads go out in one round
     const int64_t cap = int64_t(sms) * 64;
-    pack_scales_chunk_kernel<<<unsigned(std::max<int64_t>(1, std::min(cap, (L.sfa_chunks + 3) / 4))), 128, 0,
-                               stream>>>(pa);
-    pack_scales_chunk_kernel<<<unsigned(std::max<int64_t>(1, std::min(cap, (2 * L.sfb_chunks + 7) / 8))), 256, 0,
-                               stream>>>(pb);
+    const int ga = int(std::max<int64_t>(1, std::min(cap, (L.sfa_chunks + 7) / 8)));
+    const int gb = int(std::max<int64_t>(1, std::min(cap, (2 * L.sfb_chunks + 7) / 8)));
+    pack_scales_chunk_kernel<<<ga + gb, 256, 0, stream>>>(PackPair{{pa, pb}, ga});
   }
   return cuda_status(cudaGetLastError());
 }
