@@ -454,15 +454,11 @@ __device__ __forceinline__ void pack_chunks(const PackArgs& p, int bid, int nblk
     for (int j = 0; j < 4; ++j) {
       const int r = half * kBM + lane + 32 * j;
       uint32_t word = 0x7F7F7F7Fu;
-      if (p.src && r < valid) {
+      if (p.src && r < valid) {  // one word, or two joined by a funnel shift, or bytes at the edges
         const uint8_t* srow = p.src + int64_t(row0 + r) * p.src_ld;
-        word = 0;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int col = col0 + kk;
-          const uint32_t v = col < col_end ? uint32_t(__ldg(srow + col)) : 0x7Fu;
-          word |= v << (8 * kk);
-        }
+        const uintptr_t a = reinterpret_cast<uintptr_t>(srow + col0);
+        word = scale_word(srow, reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3)), uint32_t(a & 3u) * 8u,
+                          srow + p.src_ld, 0, col0, col_end);
       }
       w[j] = word;
     }
