@@ -338,6 +338,14 @@ __device__ __forceinline__ void pack_rows(const PackArgs& p, int bid, int nblk) 
   const int ks = int(threadIdx.x) / tpu, t = int(threadIdx.x) % tpu;
   const int half = t >> 5, q = t & 31;
   const int64_t chunk_bytes = p.side == 0 ? kSfaBytes : kSfbBytes;
+  // With 16-byte aligned scale rows a unit's rows are staged through shared
+  // memory in slabs of 32 k-blocks (128 bytes of each row), read with
+  // coalesced 16-byte loads, instead of each thread walking its rows word by
+  // word.  The padding column keeps the chunk reads conflict-free.
+  constexpr int kSlab = 32;
+  __shared__ uint32_t slab[2 * kBM][kSlab + 1];
+  const bool staged = p.mode == MODE_FWD && p.src != nullptr && p.src_ld % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(p.src) & 15u) == 0;
   for (int u = bid; u < units; u += nblk) {
     int e, blk;
     if (p.side == 0) {
@@ -373,6 +381,48 @@ __device__ __forceinline__ void pack_rows(const PackArgs& p, int bid, int nblk) 
     } else {
       col0 = gstart / 32;
       col_end = (gstart + glen) / 32;
+    }
+    if (staged) {
+      const int halves = p.side == 0 ? 1 : 2;
+      const int rows = halves * kBM;
+      const int warp = int(threadIdx.x) >> 5, lane = int(threadIdx.x) & 31, nwarps = int(blockDim.x) >> 5;
+      for (int kb0 = 0; kb0 < kbn; kb0 += kSlab) {
+        const int nkb = min(kSlab, kbn - kb0);
+        for (int i = int(threadIdx.x); i < rows * (kSlab / 4); i += int(blockDim.x)) {
+          const int r = i / (kSlab / 4), pc = i % (kSlab / 4);
+          const int c = col0 + kb0 * 4 + pc * 16;  // byte column of this 16-byte piece
+          uint32_t v[4] = {0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu};
+          if (r < valid && c < col_end) {
+            const uint8_t* src = p.src + int64_t(row0 + r) * p.src_ld + c;
+            if (c + 16 <= col_end) {
+              const uint4 x = __ldg(reinterpret_cast<const uint4*>(src));
+              v[0] = x.x;
+              v[1] = x.y;
+              v[2] = x.z;
+              v[3] = x.w;
+            } else {
+#pragma unroll
+              for (int b = 0; b < 16; ++b) {
+                const uint32_t byte = c + b < col_end ? uint32_t(__ldg(src + b)) : 0x7Fu;
+                v[b >> 2] = (v[b >> 2] & ~(0xFFu << (8 * (b & 3)))) | (byte << (8 * (b & 3)));
+              }
+            }
+          }
+#pragma unroll
+          for (int w = 0; w < 4; ++w) slab[r][pc * 4 + w] = v[w];
+        }
+        __syncthreads();
+        // one warp per (k-block, 128-row half): lane q stores rows q, q+32,
+        // q+64, q+96 of the half as one 16-byte piece of the chunk
+        for (int it = warp; it < nkb * halves; it += nwarps) {
+          const int kl = it / halves, h = it - kl * halves;
+          const uint4 w4 = make_uint4(slab[h * kBM + lane][kl], slab[h * kBM + lane + 32][kl],
+                                      slab[h * kBM + lane + 64][kl], slab[h * kBM + lane + 96][kl]);
+          *reinterpret_cast<uint4*>(p.dst + int64_t(chunk0 + kb0 + kl) * chunk_bytes + h * 512 + lane * 16) = w4;
+        }
+        __syncthreads();  // the slab is reloaded next
+      }
+      continue;
     }
     // per row j: start of its run, the aligned word pointer and the shift
     const uint8_t* srow[4];
